@@ -1,0 +1,497 @@
+"""Benchmark: paged decode attention (HBM GB/s) on the Llama-3-8B decode configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload ("C2"): Llama-3-8B heads (32 q / 8 kv, head_dim 128),
+block_size 16, 32 layers with their own pools, batch 64, context lengths ~ U[512, 4096],
+bf16 KV ~ N(0,1), shuffled non-contiguous block tables. One step = one decode step of the
+batch: for each of the 32 layers, reshape_and_cache of the 64 new tokens' K/V into their slots,
+then paged decode attention of the 64 queries (attention.rs:104-109 order). Each layer's pool
+(~0.6 GB) is larger than L2, so no L2 flush is needed between timed iterations.
+
+Metric value: algorithmic KV bytes read per step (sum ctx x Hkv x d x 2 [K,V] x 2 B, plus the
+q/out/table bytes) x steps x N GPUs / max-over-ranks device time. Multi-GPU: sequence sharding,
+every rank owns its own pool and batch (seed + rank); no collective on the data path ("weak").
+
+Extra objects on the same JSON line: ``roofline`` (decode kernel, live CUDA-event timing),
+``cpu_baseline`` (the oracle restatement of the reference CPU path on this host's cores),
+``e2e`` (host buffers in/out through the C ABI, copies inside the timed region), ``clocks``
+(nvidia-smi samples during the timed region), ``prefill`` (C3 varlen prefill TFLOP/s).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged decode attn HBM GB/s (% of peak) & prefill TFLOP/s at 1/2/4/8 B200"
+WORKLOAD = "C2 Llama-3-8B decode step: B=64, Hq=32, Hkv=8, d=128, bs=16, 32 layers, ctx~U[512,4096]"
+NUM_LAYERS = 32
+BATCH = 64
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=1000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch from the committed ncu summary (profiles/<name>.md), if any."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip().split()[0])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                power.append(float(r[3]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        load = [s for s, p in zip(sm, power) if p > 200.0] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# reference arm: the reference's CPU paged attention (oracle restatement), host cores only
+# ---------------------------------------------------------------------------------------
+
+def cpu_sample(seed: int, batch: int):
+    """Host-resident C2-shaped layer: the first `batch` sequences of the C2 context draw."""
+    import torch
+    from flour_b200.workloads import LLAMA8B, c2_contexts, make_decode, to_numpy
+    b = make_decode(LLAMA8B, c2_contexts(seed)[:batch], torch.bfloat16, "cpu", seed)
+    arrays = dict(q=to_numpy(b.q), kc=to_numpy(b.k_caches[0]), vc=to_numpy(b.v_caches[0]),
+                  cu=np.arange(b.num_seqs + 1, dtype=np.int32), ctx=b.ctx_host,
+                  bt=to_numpy(b.block_tables))
+    return arrays, b.kv_bytes_per_layer() + b.io_bytes_per_layer()
+
+
+def time_oracle(arrays, threads: int, reps: int, budget_s: float):
+    import oracle
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.paged_attention(arrays["q"], arrays["kc"], arrays["vc"], arrays["cu"], arrays["ctx"],
+                               arrays["bt"], 4, 1 / math.sqrt(128), dtype=oracle.DT_BF16,
+                               threads=threads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    return times
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+    threads = oracle.cpu_threads()
+    arrays, nbytes = cpu_sample(args.seed, BATCH)
+    time_oracle(arrays, threads, max(args.warmup, 0), 60.0)
+    times = time_oracle(arrays, threads, args.steps, 120.0)
+    steps = len(times)
+    total = sum(times)
+    value = nbytes * steps / total / 1e9
+    sample = (f"one layer of the C2 batch (64 seqs, {nbytes / 1e6:.0f} MB of KV) per step; "
+              "a full step is 32 such layers")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 KV, C2 shapes)", "impl": "reference",
+        "config": {"workload": WORKLOAD, "layers_per_step": 1, "batch": BATCH,
+                   "note": "reference CPU path restated in C++ (Rust reference not buildable here)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    import flour_b200  # noqa: F401  (loads libflour_attn.so, fails loudly without it)
+    from flour_b200 import ops
+    from flour_b200.workloads import LLAMA8B, c2_contexts, make_c3, make_decode
+
+    hbm_peak, tc_peak, tc_sustained, peak_kind = peaks()
+    seed = args.seed + rank
+    h = LLAMA8B
+    scale = 1.0 / math.sqrt(h.head_dim)
+    batch = make_decode(h, c2_contexts(seed), torch.bfloat16, dev, seed, num_layers=NUM_LAYERS)
+    gen = torch.Generator(device=dev).manual_seed(seed + 1)
+    B = batch.num_seqs
+    qs = [torch.randn((B, h.num_heads, h.head_dim), device=dev, generator=gen).to(torch.bfloat16)
+          for _ in range(NUM_LAYERS)]
+    knew = [torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=gen).to(torch.bfloat16)
+            for _ in range(NUM_LAYERS)]
+    vnew = [torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=gen).to(torch.bfloat16)
+            for _ in range(NUM_LAYERS)]
+    outs = [torch.empty_like(q) for q in qs]
+    ctx = batch.ctx_host
+    bt_host = batch.block_tables.cpu().numpy()
+    last = ctx - 1
+    slots = torch.tensor(bt_host[np.arange(B), last // 16] * 16 + last % 16, dtype=torch.int32,
+                         device=dev)
+    ws = ops.Workspace(dev)
+    ws.get(ops.workspace_size(B, h.num_heads, h.num_kv_heads, h.head_dim, batch.max_context_len, 1))
+    stream = torch.cuda.current_stream()
+
+    def layer_step(l, q, kn, vn, out):
+        ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], kn, vn, slots)
+        ops.paged_decode(q, batch.k_caches[l], batch.v_caches[l], batch.block_tables,
+                         batch.context_lens, h.n_rep, scale, batch.max_context_len, ws, out=out)
+
+    def step():
+        for l in range(NUM_LAYERS):
+            layer_step(l, qs[l], knew[l], vnew[l], outs[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0, "kernels reported bad device data during warm-up"
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    bytes_per_layer = batch.kv_bytes_per_layer() + batch.io_bytes_per_layer()
+    kv_bytes_step = NUM_LAYERS * bytes_per_layer
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region: K graph replays of the 32-layer decode step ----------------------
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_per_step = ms / args.steps
+    value = kv_bytes_step * args.steps * world / (ms / 1e3) / 1e9
+    assert ops.device_status() == 0
+
+    # ---- per-launch duration of the decode kernel (events on the launching stream) -------
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(NUM_LAYERS)]
+    dec_ms = []
+    for _ in range(max(2, min(args.steps, 5))):
+        for l in range(NUM_LAYERS):
+            ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], knew[l], vnew[l], slots)
+            evs[l][0].record(stream)
+            ops.paged_decode(qs[l], batch.k_caches[l], batch.v_caches[l], batch.block_tables,
+                             batch.context_lens, h.n_rep, scale, batch.max_context_len, ws,
+                             out=outs[l])
+            evs[l][1].record(stream)
+        torch.cuda.synchronize()
+        dec_ms += [a.elapsed_time(b) for a, b in evs]
+    dec_avg_ms = statistics.mean(dec_ms)
+    achieved = bytes_per_layer / (dec_avg_ms / 1e3) / 1e9
+    traffic = profile_traffic("paged_decode_c2")
+
+    # ---- e2e: host buffers through the C ABI, copies in the timed region -----------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_step,
+                      world, barrier, max_over_ranks)
+
+    # ---- prefill (C3) ------------------------------------------------------------------------
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_ranks,
+                              barrier, world)
+
+    # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------------
+    cpu = None
+    if not args.no_cpu_baseline and world == 1 and rank == 0:
+        import oracle
+        threads = oracle.cpu_threads()
+        arrays, nbytes = cpu_sample(args.seed, 16)
+        time_oracle(arrays, threads, 1, 30.0)
+        times = time_oracle(arrays, threads, 200, 10.0)
+        cpu = {"value": round(nbytes * len(times) / sum(times) / 1e9, 3), "unit": "GB/s",
+               "cores": threads, "kind": "port",
+               "sample": f"{len(times)} x one C2 layer of 16 sequences ({nbytes / 1e6:.0f} MB KV), "
+                         "oracle restatement of src/backend/cpu.rs:57-112"}
+
+    clk = clocks.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 KV and queries, random-init; C2 shapes)",
+            "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "layers": NUM_LAYERS,
+                       "parallelism": f"sequence-sharded x{world} (own pool per GPU)",
+                       "l2": "inputs larger than L2 (0.6 GB pool per layer), no flush",
+                       "kv_gb_per_step_per_gpu": round(kv_bytes_step / 1e9, 3),
+                       "hbm_frac_of_measured_peak": round(value / world / hbm_peak, 4)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "traffic": traffic, "kernel": "paged_decode_kernel<bf16,128,3>",
+                         "launch_ms": round(dec_avg_ms, 5), "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": bytes_per_layer},
+            "gpu_launches": 2 * NUM_LAYERS * args.steps,
+            "clocks": clk,
+        }
+        if e2e:
+            line["e2e"] = e2e
+        if cpu:
+            line["cpu_baseline"] = cpu
+        if prefill:
+            line["prefill"] = prefill
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_step, world,
+            barrier, max_over_ranks):
+    """Per step: the host hands per-layer q and new k/v (pinned) plus the step's metadata
+    (block tables, context lengths, slot mapping); the library writes the cache, attends and
+    the host reads every layer's output back. Copies run on a side stream, one layer ahead."""
+    B = batch.num_seqs
+    gen = torch.Generator().manual_seed(7)
+    hq = [torch.randn((B, h.num_heads, h.head_dim), generator=gen).to(torch.bfloat16).pin_memory()
+          for _ in range(NUM_LAYERS)]
+    hk = [torch.randn((B, h.num_kv_heads, h.head_dim), generator=gen).to(torch.bfloat16).pin_memory()
+          for _ in range(NUM_LAYERS)]
+    hv = [torch.randn((B, h.num_kv_heads, h.head_dim), generator=gen).to(torch.bfloat16).pin_memory()
+          for _ in range(NUM_LAYERS)]
+    ho = [torch.empty((B, h.num_heads, h.head_dim), dtype=torch.bfloat16).pin_memory()
+          for _ in range(NUM_LAYERS)]
+    h_bt = batch.block_tables.cpu().pin_memory()
+    h_ctx = batch.context_lens.cpu().pin_memory()
+    h_slots = slots.cpu().pin_memory()
+    d_bt, d_ctx, d_slots = (torch.empty_like(x, device=dev) for x in (h_bt, h_ctx, h_slots))
+    dq = [torch.empty_like(x, device=dev) for x in hq]
+    dk = [torch.empty_like(x, device=dev) for x in hk]
+    dv = [torch.empty_like(x, device=dev) for x in hv]
+    do = [torch.empty_like(x, device=dev) for x in ho]
+    copy = torch.cuda.Stream(device=dev)
+    h2d = sum(x.numel() * x.element_size() for x in (h_bt, h_ctx, h_slots)) + \
+        sum(x.numel() * x.element_size() for x in hq + hk + hv)
+    d2h = sum(x.numel() * x.element_size() for x in ho)
+
+    def one_step():
+        ev_in = []
+        with torch.cuda.stream(copy):
+            copy.wait_stream(stream)
+            d_bt.copy_(h_bt, non_blocking=True)
+            d_ctx.copy_(h_ctx, non_blocking=True)
+            d_slots.copy_(h_slots, non_blocking=True)
+            for l in range(NUM_LAYERS):
+                dq[l].copy_(hq[l], non_blocking=True)
+                dk[l].copy_(hk[l], non_blocking=True)
+                dv[l].copy_(hv[l], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(copy)
+                ev_in.append(e)
+        ev_out = []
+        for l in range(NUM_LAYERS):
+            stream.wait_event(ev_in[l])
+            ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], dk[l], dv[l], d_slots)
+            ops.paged_decode(dq[l], batch.k_caches[l], batch.v_caches[l], d_bt, d_ctx, h.n_rep,
+                             scale, batch.max_context_len, ws, out=do[l])
+            e = torch.cuda.Event()
+            e.record(stream)
+            ev_out.append(e)
+        with torch.cuda.stream(copy):
+            for l in range(NUM_LAYERS):
+                copy.wait_event(ev_out[l])
+                ho[l].copy_(do[l], non_blocking=True)
+        stream.wait_stream(copy)
+
+    for _ in range(max(args.warmup, 3)):
+        one_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        one_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    assert ops.device_status() == 0
+    return {"value": round(kv_bytes_step * args.steps * world / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(ms / args.steps, 4)}
+
+
+def run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_ranks, barrier,
+                world):
+    """C3: 16 packed sequences, shared cached prefixes; per layer reshape_and_cache of the
+    suffix K/V then causal varlen prefill over prefix+suffix. One layer's pool repeated."""
+    b = make_c3(dev, seed=seed + 3)
+    h = b.heads
+    scale = 1.0 / math.sqrt(h.head_dim)
+    ws = ops.Workspace(dev)
+
+    def layer():
+        ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
+        return ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                                 b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len,
+                                 ws)
+
+    out = layer()
+    torch.cuda.synchronize()
+    reps = 8
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        layer()
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(stream)
+    for _ in range(reps):
+        layer()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
+    p0.record(stream)
+    ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                      b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len, ws,
+                      out=out)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+    kernel_ms = p0.elapsed_time(p1)
+    flops = b.flops()
+    return {"config": "C3 varlen causal prefill, 16 seqs L~U[128,2048], groups of 4 sharing "
+                      "0-50% cached prefixes, Llama-3-8B heads, bf16",
+            "tflops": round(flops * world / (ms / 1e3) / 1e12, 2),
+            "kernel_tflops": round(flops / (kernel_ms / 1e3) / 1e12, 2),
+            "frac_of_measured_peak": round(flops / (kernel_ms / 1e3) / 1e12 / tc_peak, 4),
+            "ms_per_layer": round(ms, 4), "suffix_tokens": int(b.q.shape[0]),
+            "flops_per_layer": flops}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,490 @@
+// C ABI of libflour_attn.so: host-side validation, launch planning and dispatch to the
+// sm_100a kernels. See include/flour_attn.h for the contract of every entry point.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "attn_generic.cuh"
+#include "cache_ops.cuh"
+#include "decode_sm100.cuh"
+#include "flour_attn.h"
+
+namespace {
+
+thread_local char g_msg[512];
+
+fa_status fail(fa_status st, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+fa_status ok() {
+  g_msg[0] = '\0';
+  return FA_OK;
+}
+
+fa_status check_launch(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+int dtype_size(int32_t dt) { return dt == FA_F32 ? 4 : 2; }
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+fa_status check_layer(const fa_kv_layer *L, const char *who) {
+  if (!L) return fail(FA_EINVAL, "%s: layer is NULL", who);
+  if (!L->k_cache || !L->v_cache) return fail(FA_EINVAL, "%s: k_cache/v_cache is NULL", who);
+  if (L->dtype != FA_F32 && L->dtype != FA_BF16 && L->dtype != FA_F16)
+    return fail(FA_EINVAL, "%s: unknown dtype %d", who, L->dtype);
+  if (L->num_blocks <= 0 || L->num_kv_heads <= 0 || L->block_size <= 0 || L->head_dim <= 0)
+    return fail(FA_EINVAL, "%s: layer dims must be positive (blocks=%d kv_heads=%d bs=%d d=%d)",
+                who, L->num_blocks, L->num_kv_heads, L->block_size, L->head_dim);
+  return FA_OK;
+}
+
+// ---- tensor maps ----------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+fa_status get_encoder() {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(FA_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return FA_OK;
+}
+
+// 2-D map over one K or V slab viewed as [rows = num_blocks*kv_heads*block_size, head_dim],
+// box = 16 rows x 64 elements (128 B), 128-byte swizzle.
+fa_status make_page_map(CUtensorMap *map, void *base, int64_t rows, int head_dim, int32_t dt) {
+  if (fa_status s = get_encoder(); s != FA_OK) return s;
+  const CUtensorMapDataType t =
+      dt == FA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {cuuint64_t(head_dim), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(head_dim) * 2};
+  cuuint32_t box[2] = {64, 16};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, t, 2, base, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return FA_OK;
+}
+
+// ---- decode planning --------------------------------------------------------------------
+
+constexpr int kSmCount = 148;
+constexpr int kDecodeCtasPerSm = 2;
+
+struct DecodePlan {
+  int pages_per_split = 0;
+  int max_splits = 0;
+};
+
+// Split the context so that about four waves of CTAs cover the whole GPU, with at least 16
+// pages per split (4 per warp) and at most kDecodeMaxPagesPerSplit.
+bool plan_decode(int num_seqs, int num_kv_heads, int max_context_len, DecodePlan *out) {
+  const int max_pages = (max_context_len + fa::kPage - 1) / fa::kPage;
+  const long units = long(num_seqs) * num_kv_heads;
+  const long target = long(kSmCount) * kDecodeCtasPerSm * 4;
+  const long want = std::max(1L, (target + units - 1) / units);
+  int pps = int((max_pages + want - 1) / want);
+  pps = std::max(pps, 16);
+  pps = (pps + 3) / 4 * 4;
+  pps = std::min(pps, fa::kDecodeMaxPagesPerSplit);
+  const int splits = (max_pages + pps - 1) / pps;
+  if (splits > fa::kDecodeMaxSplits) return false;
+  out->pages_per_split = pps;
+  out->max_splits = std::max(splits, 1);
+  return true;
+}
+
+struct DecodeWorkspace {
+  size_t counters_off, lse_off, o_off, bytes;
+};
+
+DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                                        const DecodePlan &plan) {
+  auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
+  DecodeWorkspace w{};
+  if (plan.max_splits <= 1) return w;
+  w.counters_off = 0;
+  w.lse_off = r256(size_t(num_seqs) * num_kv_heads * 4);
+  w.o_off = w.lse_off + r256(size_t(num_seqs) * num_heads * plan.max_splits * 4);
+  w.bytes = w.o_off + size_t(num_seqs) * num_heads * plan.max_splits * head_dim * 4;
+  return w;
+}
+
+bool decode_fast_path(const fa_kv_layer *L, int n_rep, const void *q, const void *out) {
+  return (L->dtype == FA_BF16 || L->dtype == FA_F16) && L->block_size == fa::kPage &&
+         (L->head_dim == 64 || L->head_dim == 128) && n_rep >= 1 && n_rep <= 8 &&
+         int64_t(L->num_blocks) * L->num_kv_heads * L->block_size < (int64_t(1) << 31) &&
+         aligned(L->k_cache, 16) && aligned(L->v_cache, 16) && aligned(q, 16) &&
+         aligned(out, 16);
+}
+
+template <typename T, int HD, int NSTAGE>
+fa_status launch_decode_t(const fa::DecodeParams &p, const CUtensorMap &tk, const CUtensorMap &tv,
+                          cudaStream_t stream) {
+  using S = fa::DecodeSmem<HD, NSTAGE>;
+  auto kern = fa::paged_decode_kernel<T, HD, NSTAGE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "decode: set smem attribute: %s", cudaGetErrorString(e));
+  dim3 grid(p.max_splits, p.num_kv_heads, p.num_seqs);
+  kern<<<grid, fa::kDecodeThreads, S::kAlloc, stream>>>(p, tk, tv);
+  return check_launch("paged_decode");
+}
+
+constexpr int kDecodeStages = 3;
+
+fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const int32_t *ctx,
+                        const int32_t *tables, int max_blocks, int num_seqs, int num_heads,
+                        int n_rep, int max_context_len, float scale, void *ws, size_t ws_bytes,
+                        cudaStream_t stream) {
+  DecodePlan plan;
+  if (!plan_decode(num_seqs, L->num_kv_heads, max_context_len, &plan))
+    return fail(FA_EUNSUPPORTED, "decode: context of %d tokens needs more than %d splits",
+                max_context_len, fa::kDecodeMaxSplits);
+  const DecodeWorkspace w =
+      decode_workspace_layout(num_seqs, num_heads, L->num_kv_heads, L->head_dim, plan);
+  if (w.bytes > 0) {
+    if (!ws) return fail(FA_EINVAL, "decode: workspace is NULL but %zu bytes are needed", w.bytes);
+    if (ws_bytes < w.bytes)
+      return fail(FA_ERANGE, "decode: workspace of %zu bytes, %zu needed", ws_bytes, w.bytes);
+    if (!aligned(ws, 256)) return fail(FA_EINVAL, "decode: workspace must be 256-byte aligned");
+  }
+  fa::DecodeParams p{};
+  p.q = q;
+  p.out = out;
+  p.context_lens = ctx;
+  p.block_tables = tables;
+  char *wsb = static_cast<char *>(ws);
+  p.counters = w.bytes ? reinterpret_cast<int32_t *>(wsb + w.counters_off) : nullptr;
+  p.part_lse = w.bytes ? reinterpret_cast<float *>(wsb + w.lse_off) : nullptr;
+  p.part_o = w.bytes ? reinterpret_cast<float *>(wsb + w.o_off) : nullptr;
+  p.max_blocks_per_seq = max_blocks;
+  p.num_seqs = num_seqs;
+  p.num_heads = num_heads;
+  p.num_kv_heads = L->num_kv_heads;
+  p.n_rep = n_rep;
+  p.num_blocks = L->num_blocks;
+  p.pages_per_split = plan.pages_per_split;
+  p.max_splits = plan.max_splits;
+  p.max_context_len = max_context_len;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t rows = int64_t(L->num_blocks) * L->num_kv_heads * L->block_size;
+  CUtensorMap tk, tv;
+  if (fa_status s = make_page_map(&tk, L->k_cache, rows, L->head_dim, L->dtype); s != FA_OK) return s;
+  if (fa_status s = make_page_map(&tv, L->v_cache, rows, L->head_dim, L->dtype); s != FA_OK) return s;
+  if (L->dtype == FA_BF16) {
+    if (L->head_dim == 128) return launch_decode_t<__nv_bfloat16, 128, kDecodeStages>(p, tk, tv, stream);
+    return launch_decode_t<__nv_bfloat16, 64, kDecodeStages>(p, tk, tv, stream);
+  }
+  if (L->head_dim == 128) return launch_decode_t<__half, 128, kDecodeStages>(p, tk, tv, stream);
+  return launch_decode_t<__half, 64, kDecodeStages>(p, tk, tv, stream);
+}
+
+fa_status launch_generic(const fa_kv_layer *L, const void *q, void *out, const int32_t *cu,
+                         const int32_t *ctx, const int32_t *tables, int max_blocks, int num_seqs,
+                         int num_heads, int n_rep, int total_q, float scale, cudaStream_t stream) {
+  if (L->head_dim > fa::kGenericMaxDim)
+    return fail(FA_EUNSUPPORTED, "head_dim %d > %d is not supported", L->head_dim, fa::kGenericMaxDim);
+  if (L->block_size > 1024)
+    return fail(FA_EUNSUPPORTED, "block_size %d > 1024 is not supported", L->block_size);
+  fa::GenericParams p{};
+  p.q = q;
+  p.out = out;
+  p.k_cache = L->k_cache;
+  p.v_cache = L->v_cache;
+  p.cu_seqlens_q = cu;
+  p.context_lens = ctx;
+  p.block_tables = tables;
+  p.max_blocks_per_seq = max_blocks;
+  p.num_seqs = num_seqs;
+  p.num_heads = num_heads;
+  p.num_kv_heads = L->num_kv_heads;
+  p.n_rep = n_rep;
+  p.head_dim = L->head_dim;
+  p.block_size = L->block_size;
+  p.num_blocks = L->num_blocks;
+  p.total_q = total_q;
+  p.scale = scale;
+  const size_t smem = (fa::kGenericMaxDim + L->block_size) * sizeof(float);
+  dim3 grid(total_q, num_heads);
+  switch (L->dtype) {
+    case FA_F32: fa::generic_attn_kernel<float><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
+    case FA_BF16: fa::generic_attn_kernel<__nv_bfloat16><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
+    default: fa::generic_attn_kernel<__half><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
+  }
+  return check_launch("paged_attention (generic)");
+}
+
+fa_status check_attention_args(const char *who, const fa_kv_layer *L, const void *q, const void *out,
+                               const int32_t *ctx, const int32_t *tables, int max_blocks,
+                               int num_seqs, int num_heads, int n_rep, int max_context_len,
+                               float scale) {
+  if (fa_status s = check_layer(L, who); s != FA_OK) return s;
+  if (!q || !out || !ctx || !tables) return fail(FA_EINVAL, "%s: NULL query/out/context_lens/block_tables", who);
+  if (num_seqs < 0 || max_blocks <= 0) return fail(FA_EINVAL, "%s: num_seqs=%d max_blocks_per_seq=%d", who, num_seqs, max_blocks);
+  if (n_rep <= 0 || num_heads != n_rep * L->num_kv_heads)
+    return fail(FA_EINVAL, "%s: num_heads (%d) must equal n_rep (%d) * num_kv_heads (%d)", who,
+                num_heads, n_rep, L->num_kv_heads);
+  if (max_context_len < 0 || int64_t(max_context_len) > int64_t(max_blocks) * L->block_size)
+    return fail(FA_ERANGE, "%s: max_context_len %d outside [0, %lld]", who, max_context_len,
+                (long long)max_blocks * L->block_size);
+  if (!std::isfinite(scale)) return fail(FA_EINVAL, "%s: scale is not finite", who);
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t fa_abi_version(void) { return 1; }
+
+const char *fa_status_string(int32_t s) {
+  switch (s) {
+    case FA_OK: return "ok";
+    case FA_EINVAL: return "invalid argument";
+    case FA_ERANGE: return "out of range";
+    case FA_ECUDA: return "CUDA error";
+    case FA_ETIMEOUT: return "device wait timed out";
+    case FA_EUNSUPPORTED: return "unsupported configuration";
+    case FA_EDEVICE: return "kernel reported bad device data";
+    default: return "unknown status";
+  }
+}
+
+const char *fa_last_error_message(void) { return g_msg; }
+
+fa_status fa_device_status(int32_t *status_out, int32_t clear, fa_stream_t stream) {
+  if (!status_out) return fail(FA_EINVAL, "device_status: status_out is NULL");
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "device_status: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, fa::g_status, sizeof(int));
+  if (e != cudaSuccess) return fail(FA_ECUDA, "device_status: %s", cudaGetErrorString(e));
+  if (clear) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(fa::g_status, &z, sizeof(int));
+    if (e != cudaSuccess) return fail(FA_ECUDA, "device_status: %s", cudaGetErrorString(e));
+  }
+  *status_out = v;
+  if (v & FA_DEVERR_TIMEOUT) return fail(FA_ETIMEOUT, "a device-side wait timed out (0x%x)", v);
+  if (v) return fail(FA_EDEVICE, "kernels reported bad device data (0x%x)", v);
+  return ok();
+}
+
+fa_status fa_reshape_and_cache(const fa_kv_layer *layer, const void *key, const void *value,
+                               int64_t key_stride_token, int64_t key_stride_head,
+                               int64_t value_stride_token, int64_t value_stride_head,
+                               const int32_t *slot_mapping, int32_t num_tokens,
+                               fa_stream_t stream) {
+  if (fa_status s = check_layer(layer, "reshape_and_cache"); s != FA_OK) return s;
+  if (num_tokens < 0) return fail(FA_EINVAL, "reshape_and_cache: num_tokens < 0");
+  if (num_tokens == 0) return ok();
+  if (!key || !value || !slot_mapping)
+    return fail(FA_EINVAL, "reshape_and_cache: NULL key/value/slot_mapping");
+  const int es = dtype_size(layer->dtype);
+  fa::ReshapeParams p{};
+  p.key = static_cast<const char *>(key);
+  p.value = static_cast<const char *>(value);
+  p.k_cache = static_cast<char *>(layer->k_cache);
+  p.v_cache = static_cast<char *>(layer->v_cache);
+  p.slot_mapping = slot_mapping;
+  p.key_stride_token = key_stride_token * es;
+  p.key_stride_head = key_stride_head * es;
+  p.value_stride_token = value_stride_token * es;
+  p.value_stride_head = value_stride_head * es;
+  p.num_slots = int64_t(layer->num_blocks) * layer->block_size;
+  p.num_tokens = num_tokens;
+  p.num_kv_heads = layer->num_kv_heads;
+  p.block_size = layer->block_size;
+  p.row_bytes = layer->head_dim * es;
+  // Widest vector every address and stride allows.
+  int vec = 16;
+  auto fits = [&](int v) {
+    return p.row_bytes % v == 0 && aligned(key, v) && aligned(value, v) &&
+           aligned(layer->k_cache, v) && aligned(layer->v_cache, v) && p.key_stride_token % v == 0 &&
+           p.key_stride_head % v == 0 && p.value_stride_token % v == 0 &&
+           p.value_stride_head % v == 0;
+  };
+  while (vec > 2 && !fits(vec)) vec >>= 1;
+  if (!fits(vec)) return fail(FA_EINVAL, "reshape_and_cache: misaligned key/value/cache");
+  const int64_t items = int64_t(num_tokens) * layer->num_kv_heads * (p.row_bytes / vec);
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((items + threads - 1) / threads, int64_t(kSmCount) * 16);
+  switch (vec) {
+    case 16: fa::reshape_and_cache_kernel<16><<<unsigned(blocks), threads, 0, stream>>>(p); break;
+    case 8: fa::reshape_and_cache_kernel<8><<<unsigned(blocks), threads, 0, stream>>>(p); break;
+    case 4: fa::reshape_and_cache_kernel<4><<<unsigned(blocks), threads, 0, stream>>>(p); break;
+    default: fa::reshape_and_cache_kernel<2><<<unsigned(blocks), threads, 0, stream>>>(p); break;
+  }
+  return check_launch("reshape_and_cache");
+}
+
+fa_status fa_copy_blocks(const fa_kv_layer *layers, int32_t num_layers, const int32_t *block_mapping,
+                         int32_t num_pairs, fa_stream_t stream) {
+  if (!layers) return fail(FA_EINVAL, "copy_blocks: layers is NULL");
+  if (num_layers <= 0 || num_layers > FA_MAX_COPY_LAYERS)
+    return fail(FA_EINVAL, "copy_blocks: num_layers %d outside [1, %d]", num_layers, FA_MAX_COPY_LAYERS);
+  if (num_pairs < 0) return fail(FA_EINVAL, "copy_blocks: num_pairs < 0");
+  if (num_pairs == 0) return ok();
+  if (!block_mapping) return fail(FA_EINVAL, "copy_blocks: block_mapping is NULL");
+  fa::CopyParams p{};
+  const fa_kv_layer &L0 = layers[0];
+  for (int l = 0; l < num_layers; ++l) {
+    if (fa_status s = check_layer(&layers[l], "copy_blocks"); s != FA_OK) return s;
+    const fa_kv_layer &L = layers[l];
+    if (L.num_blocks != L0.num_blocks || L.num_kv_heads != L0.num_kv_heads ||
+        L.block_size != L0.block_size || L.head_dim != L0.head_dim || L.dtype != L0.dtype)
+      return fail(FA_EINVAL, "copy_blocks: layer %d shape/dtype differs from layer 0", l);
+    p.k[l] = static_cast<char *>(L.k_cache);
+    p.v[l] = static_cast<char *>(L.v_cache);
+  }
+  p.pairs = block_mapping;
+  p.num_pairs = num_pairs;
+  p.num_blocks = L0.num_blocks;
+  p.block_bytes = int64_t(L0.num_kv_heads) * L0.block_size * L0.head_dim * dtype_size(L0.dtype);
+  int vec = 16;
+  auto fits = [&](int v) {
+    if (p.block_bytes % v) return false;
+    for (int l = 0; l < num_layers; ++l)
+      if (!aligned(p.k[l], v) || !aligned(p.v[l], v)) return false;
+    return true;
+  };
+  while (vec > 2 && !fits(vec)) vec >>= 1;
+  if (!fits(vec)) return fail(FA_EINVAL, "copy_blocks: misaligned caches");
+  dim3 grid(num_pairs, num_layers, 2);
+  switch (vec) {
+    case 16: fa::copy_blocks_kernel<16><<<grid, 256, 0, stream>>>(p); break;
+    case 8: fa::copy_blocks_kernel<8><<<grid, 256, 0, stream>>>(p); break;
+    case 4: fa::copy_blocks_kernel<4><<<grid, 256, 0, stream>>>(p); break;
+    default: fa::copy_blocks_kernel<2><<<grid, 256, 0, stream>>>(p); break;
+  }
+  return check_launch("copy_blocks");
+}
+
+static fa_status block_copy(const fa_kv_layer *layer, int32_t block_id, void *kdst, const void *ksrc,
+                            void *vdst, const void *vsrc, cudaStream_t stream, const char *who) {
+  const size_t bytes =
+      size_t(layer->num_kv_heads) * layer->block_size * layer->head_dim * dtype_size(layer->dtype);
+  cudaError_t e = cudaMemcpyAsync(kdst, ksrc, bytes, cudaMemcpyDefault, stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(vdst, vsrc, bytes, cudaMemcpyDefault, stream);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: %s", who, cudaGetErrorString(e));
+  (void)block_id;
+  return ok();
+}
+
+fa_status fa_write_block(const fa_kv_layer *layer, int32_t block_id, const void *key, const void *value,
+                         fa_stream_t stream) {
+  if (fa_status s = check_layer(layer, "write_block"); s != FA_OK) return s;
+  if (!key || !value) return fail(FA_EINVAL, "write_block: NULL key/value");
+  if (block_id < 0 || block_id >= layer->num_blocks)
+    return fail(FA_ERANGE, "write_block: block_id %d outside [0, %d)", block_id, layer->num_blocks);
+  const size_t off =
+      size_t(block_id) * layer->num_kv_heads * layer->block_size * layer->head_dim * dtype_size(layer->dtype);
+  return block_copy(layer, block_id, static_cast<char *>(layer->k_cache) + off, key,
+                    static_cast<char *>(layer->v_cache) + off, value, stream, "write_block");
+}
+
+fa_status fa_read_block(const fa_kv_layer *layer, int32_t block_id, void *key, void *value,
+                        fa_stream_t stream) {
+  if (fa_status s = check_layer(layer, "read_block"); s != FA_OK) return s;
+  if (!key || !value) return fail(FA_EINVAL, "read_block: NULL key/value");
+  if (block_id < 0 || block_id >= layer->num_blocks)
+    return fail(FA_ERANGE, "read_block: block_id %d outside [0, %d)", block_id, layer->num_blocks);
+  const size_t off =
+      size_t(block_id) * layer->num_kv_heads * layer->block_size * layer->head_dim * dtype_size(layer->dtype);
+  return block_copy(layer, block_id, key, static_cast<const char *>(layer->k_cache) + off, value,
+                    static_cast<const char *>(layer->v_cache) + off, stream, "read_block");
+}
+
+size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                                         int32_t head_dim, int32_t max_context_len,
+                                         int32_t max_seqlen_q) {
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_context_len <= 0)
+    return 0;
+  if (max_seqlen_q != 1) return 0;
+  DecodePlan plan;
+  if (!plan_decode(num_seqs, num_kv_heads, max_context_len, &plan)) return 0;
+  return decode_workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, plan).bytes;
+}
+
+fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, void *out,
+                          const int32_t *context_lens, const int32_t *block_tables,
+                          int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
+                          int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
+                          size_t workspace_bytes, fa_stream_t stream) {
+  if (fa_status s = check_attention_args("paged_decode", layer, query, out, context_lens,
+                                         block_tables, max_blocks_per_seq, num_seqs, num_heads,
+                                         n_rep, max_context_len, scale);
+      s != FA_OK)
+    return s;
+  if (num_seqs == 0) return ok();
+  if (max_context_len < 1) return fail(FA_ERANGE, "paged_decode: max_context_len must be >= 1");
+  if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "paged_decode: more than 65535 sequences per call");
+  if (decode_fast_path(layer, n_rep, query, out))
+    return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq,
+                         num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                         workspace_bytes, stream);
+  return launch_generic(layer, query, out, nullptr, context_lens, block_tables, max_blocks_per_seq,
+                        num_seqs, num_heads, n_rep, num_seqs, scale, stream);
+}
+
+fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *out,
+                           const int32_t *cu_seqlens_q, const int32_t *context_lens,
+                           const int32_t *block_tables, int32_t max_blocks_per_seq, int32_t num_seqs,
+                           int32_t num_heads, int32_t n_rep, int32_t total_q, int32_t max_seqlen_q,
+                           int32_t max_context_len, float scale, void *workspace,
+                           size_t workspace_bytes, fa_stream_t stream) {
+  if (fa_status s = check_attention_args("paged_prefill", layer, query, out, context_lens,
+                                         block_tables, max_blocks_per_seq, num_seqs, num_heads,
+                                         n_rep, max_context_len, scale);
+      s != FA_OK)
+    return s;
+  if (!cu_seqlens_q) return fail(FA_EINVAL, "paged_prefill: cu_seqlens_q is NULL");
+  if (total_q < 0 || max_seqlen_q < 0) return fail(FA_EINVAL, "paged_prefill: negative total_q/max_seqlen_q");
+  if (max_seqlen_q > max_context_len)
+    return fail(FA_ERANGE, "paged_prefill: max_seqlen_q %d > max_context_len %d", max_seqlen_q, max_context_len);
+  (void)workspace;
+  (void)workspace_bytes;
+  if (total_q == 0 || num_seqs == 0) return ok();
+  return launch_generic(layer, query, out, cu_seqlens_q, context_lens, block_tables,
+                        max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, stream);
+}
+
+fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query, void *out,
+                             const int32_t *cu_seqlens_q, const int32_t *context_lens,
+                             const int32_t *block_tables, int32_t max_blocks_per_seq,
+                             int32_t num_seqs, int32_t num_heads, int32_t n_rep, int32_t total_q,
+                             int32_t max_seqlen_q, int32_t max_context_len, float scale,
+                             void *workspace, size_t workspace_bytes, fa_stream_t stream) {
+  // Every sequence has exactly one query token when total_q == num_seqs and none has more
+  // than one: that is the decode specialisation.
+  if (max_seqlen_q == 1 && total_q == num_seqs)
+    return fa_paged_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq,
+                           num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                           workspace_bytes, stream);
+  return fa_paged_prefill(layer, query, out, cu_seqlens_q, context_lens, block_tables,
+                          max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, max_seqlen_q,
+                          max_context_len, scale, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,192 @@
+"""torch-facing wrappers over the C ABI (device memory and streams come from torch).
+
+Every function here calls exactly one ``fa_*`` entry point of libflour_attn.so on the current
+torch CUDA stream; there is no Python compute path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import FaKvLayer, check, lib
+
+_DTYPES = {torch.float32: _lib.FA_F32, torch.bfloat16: _lib.FA_BF16, torch.float16: _lib.FA_F16}
+
+
+def fa_dtype(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"unsupported dtype {dtype}") from None
+
+
+def _stream(stream=None):
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def layer_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> FaKvLayer:
+    """``fa_kv_layer`` for one layer's slabs of shape [num_blocks, kv_heads, bs, head_dim]."""
+    if k_cache.shape != v_cache.shape or k_cache.dtype != v_cache.dtype:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "k_cache and v_cache differ in shape or dtype")
+    if k_cache.dim() != 4 or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise _lib.FlourAttnError(_lib.FA_EINVAL,
+                                  "cache slabs must be contiguous [num_blocks, kv_heads, bs, d]")
+    nb, kvh, bs, d = k_cache.shape
+    return FaKvLayer(k_cache.data_ptr(), v_cache.data_ptr(), nb, kvh, bs, d, fa_dtype(k_cache.dtype))
+
+
+def _i32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.int32 or not t.is_contiguous():
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"{name} must be a contiguous int32 tensor")
+    return t
+
+
+# ---- block writes / copies ----------------------------------------------------------------
+
+def reshape_and_cache(k_cache, v_cache, key, value, slot_mapping, stream=None) -> None:
+    """Scatter key/value rows [T, kv_heads, d] (any token/head strides, unit stride on d) into
+    their pool slots; slot -1 skips a token. PagedKvPool::write, paged.rs:186-204."""
+    layer = layer_desc(k_cache, v_cache)
+    if key.stride(-1) != 1 or value.stride(-1) != 1:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "key/value need unit stride on head_dim")
+    if key.dtype != k_cache.dtype or value.dtype != k_cache.dtype:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "key/value dtype differs from the pool dtype")
+    sm = _i32(slot_mapping, "slot_mapping")
+    check(lib().fa_reshape_and_cache(ctypes.byref(layer), _ptr(key), _ptr(value), key.stride(0),
+                                     key.stride(1), value.stride(0), value.stride(1), _ptr(sm),
+                                     sm.numel(), _stream(stream)), "reshape_and_cache")
+
+
+def copy_blocks(k_caches, v_caches, block_mapping, stream=None) -> None:
+    """Copy whole blocks (src, dst) = block_mapping[i] in every layer, K and V."""
+    layers = (FaKvLayer * len(k_caches))(*[layer_desc(k, v) for k, v in zip(k_caches, v_caches)])
+    bm = _i32(block_mapping, "block_mapping")
+    check(lib().fa_copy_blocks(layers, len(k_caches), _ptr(bm), bm.numel() // 2, _stream(stream)),
+          "copy_blocks")
+
+
+def write_block(k_cache, v_cache, block_id: int, key, value, stream=None) -> None:
+    """PagedKvPool::write_block: key/value (kv_heads, bs, d), host (pinned or not) or device."""
+    layer = layer_desc(k_cache, v_cache)
+    check(lib().fa_write_block(ctypes.byref(layer), block_id, _ptr(key.contiguous()),
+                               _ptr(value.contiguous()), _stream(stream)), "write_block")
+
+
+def read_block(k_cache, v_cache, block_id: int, key_out, value_out, stream=None) -> None:
+    layer = layer_desc(k_cache, v_cache)
+    check(lib().fa_read_block(ctypes.byref(layer), block_id, _ptr(key_out), _ptr(value_out),
+                              _stream(stream)), "read_block")
+
+
+# ---- attention ----------------------------------------------------------------------------
+
+def workspace_size(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                   max_context_len: int, max_seqlen_q: int) -> int:
+    return int(lib().fa_paged_attention_workspace_size(num_seqs, num_heads, num_kv_heads,
+                                                       head_dim, max_context_len, max_seqlen_q))
+
+
+class Workspace:
+    """Caller-owned, zero-initialised scratch for the split-K partials (grown on demand).
+    One Workspace per stream: concurrent calls must not share it."""
+
+    def __init__(self, device=None):
+        self.device = torch.device(device if device is not None else "cuda")
+        self.buf: torch.Tensor | None = None
+
+    def get(self, nbytes: int) -> torch.Tensor | None:
+        if nbytes == 0:
+            return self.buf
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def _ws_args(ws: Workspace | None, need: int):
+    if need == 0:
+        return None, 0
+    if ws is None:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"a workspace of {need} bytes is required")
+    buf = ws.get(need)
+    return _ptr(buf), buf.numel()
+
+
+def paged_decode(query, k_cache, v_cache, block_tables, context_lens, n_rep: int, scale: float,
+                 max_context_len: int, workspace: Workspace | None = None, out=None,
+                 stream=None):
+    """One query token per sequence: query [B, Hq, d] -> out [B, Hq, d]."""
+    layer = layer_desc(k_cache, v_cache)
+    query = query.contiguous()
+    out = torch.empty_like(query) if out is None else out
+    bt, cl = _i32(block_tables, "block_tables"), _i32(context_lens, "context_lens")
+    B, hq, d = query.shape
+    need = workspace_size(B, hq, k_cache.shape[1], d, max_context_len, 1)
+    wp, wn = _ws_args(workspace, need)
+    check(lib().fa_paged_decode(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cl), _ptr(bt),
+                                bt.shape[1], B, hq, n_rep, max_context_len, scale, wp, wn,
+                                _stream(stream)), "paged_decode")
+    return out
+
+
+def paged_prefill(query, k_cache, v_cache, cu_seqlens_q, context_lens, block_tables, n_rep: int,
+                  scale: float, max_seqlen_q: int, max_context_len: int,
+                  workspace: Workspace | None = None, out=None, stream=None):
+    """Varlen causal attention of packed suffix queries [Tq, Hq, d] over prefix+suffix KV."""
+    layer = layer_desc(k_cache, v_cache)
+    query = query.contiguous()
+    out = torch.empty_like(query) if out is None else out
+    cu = _i32(cu_seqlens_q, "cu_seqlens_q")
+    bt, cl = _i32(block_tables, "block_tables"), _i32(context_lens, "context_lens")
+    tq, hq, d = query.shape
+    S = cl.numel()
+    need = workspace_size(S, hq, k_cache.shape[1], d, max_context_len, max_seqlen_q)
+    wp, wn = _ws_args(workspace, need)
+    check(lib().fa_paged_prefill(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cu), _ptr(cl),
+                                 _ptr(bt), bt.shape[1], S, hq, n_rep, tq, max_seqlen_q,
+                                 max_context_len, scale, wp, wn, _stream(stream)), "paged_prefill")
+    return out
+
+
+def paged_attention_varlen(query, k_cache, v_cache, cu_seqlens_q, context_lens, block_tables,
+                           n_rep: int, scale: float, max_seqlen_q: int, max_context_len: int,
+                           workspace: Workspace | None = None, out=None, stream=None):
+    """The general entry (fa_paged_attention): decode or prefill chosen by the library."""
+    layer = layer_desc(k_cache, v_cache)
+    query = query.contiguous()
+    out = torch.empty_like(query) if out is None else out
+    cu = _i32(cu_seqlens_q, "cu_seqlens_q")
+    bt, cl = _i32(block_tables, "block_tables"), _i32(context_lens, "context_lens")
+    tq, hq, d = query.shape
+    S = cl.numel()
+    need = workspace_size(S, hq, k_cache.shape[1], d, max_context_len,
+                          1 if (max_seqlen_q == 1 and tq == S) else max_seqlen_q)
+    wp, wn = _ws_args(workspace, need)
+    check(lib().fa_paged_attention(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cu), _ptr(cl),
+                                   _ptr(bt), bt.shape[1], S, hq, n_rep, tq, max_seqlen_q,
+                                   max_context_len, scale, wp, wn, _stream(stream)),
+          "paged_attention")
+    return out
+
+
+def device_status(clear: bool = True, stream=None) -> int:
+    """FA_DEVERR_* bits the kernels reported on the current device (waits for the stream)."""
+    v = ctypes.c_int32(0)
+    st = lib().fa_device_status(ctypes.byref(v), 1 if clear else 0, _stream(stream))
+    if st not in (_lib.FA_OK, _lib.FA_EDEVICE, _lib.FA_ETIMEOUT):
+        check(st, "device_status")
+    return int(v.value)
+
+
+def default_scale(head_dim: int) -> float:
+    """1/sqrt(head_dim), the scale attention.rs:108 passes."""
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,62 @@
+"""Small, fixed cases for Nsight Compute captures of one kernel.
+
+    python -m flour_b200.profile_case decode  [--launches 3] [--batch 64] [--seed 1000]
+    python -m flour_b200.profile_case longctx [--launches 3]
+    python -m flour_b200.profile_case prefill [--launches 3]
+
+`decode` is one layer of the C2 configuration (64 sequences, ctx ~ U[512, 4096], ~0.6 GB of
+KV: larger than L2, a few GB at most on the device). `longctx` is 4 sequences of the C4
+distribution (split-K heavy). `prefill` is one layer of C3. Each case runs one warm-up launch
+and then `--launches` launches of the kernel under test, and exits 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+
+import numpy as np
+import torch
+
+from . import ops
+from .workloads import LLAMA8B, c2_contexts, c4_contexts, make_c3, make_decode
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["decode", "longctx", "prefill"])
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--seed", type=int, default=1000)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    scale = 1.0 / math.sqrt(128)
+    if a.case in ("decode", "longctx"):
+        ctx = c2_contexts(a.seed, a.batch) if a.case == "decode" else c4_contexts(a.seed, 4)
+        b = make_decode(LLAMA8B, ctx, torch.bfloat16, dev, a.seed)
+        ws = ops.Workspace(dev)
+        out = torch.empty_like(b.q)
+        for _ in range(1 + a.launches):
+            ops.paged_decode(b.q, b.k_caches[0], b.v_caches[0], b.block_tables, b.context_lens, 4,
+                             scale, b.max_context_len, ws, out=out)
+        torch.cuda.synchronize()
+        print(f"{a.case}: {b.kv_bytes_per_layer() + b.io_bytes_per_layer()} algorithmic bytes/launch")
+    else:
+        b = make_c3(dev, seed=a.seed)
+        ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
+        ws = ops.Workspace(dev)
+        out = torch.empty_like(b.q)
+        for _ in range(1 + a.launches):
+            ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                              b.block_tables, 4, scale, b.max_seqlen_q, b.max_context_len, ws,
+                              out=out)
+        torch.cuda.synchronize()
+        print(f"prefill: {b.flops()} algorithmic FLOPs/launch")
+    st = ops.device_status()
+    if st:
+        raise SystemExit(f"device status 0x{st:x}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,184 @@
+/*
+ * flour_attn.h — C ABI of the B200 (sm_100a) paged KV pool + paged attention backend for flour.
+ *
+ * The reference (lltsdyp/flour, Rust, CPU-only) has no FFI for this path; its boundary is the
+ * trio called from src/models/common/attention.rs:104-109:
+ *
+ *     Cache::write_kv(layer, k (1,Hkv,n,d), v)                 src/models/common/cache.rs:451
+ *     Cache::kv_blocks(layer) -> Vec<(K,V) block views>          src/models/common/cache.rs:456
+ *     backend::cpu::paged_attention(q, blocks, n_rep, scale)     src/backend/cpu.rs:57
+ *
+ * Each entry point below names the reference function it replaces. Everything here uses plain
+ * pointers, sizes and a CUDA stream handle: no Rust, torch or candle types cross the boundary.
+ *
+ * Conventions
+ *   - Device memory (pools, queries, outputs, tables, workspace) is owned by the caller. No
+ *     entry point allocates device memory.
+ *   - Every call is ordered on `stream` and returns before the GPU work finishes.
+ *   - Host-side argument checks return FA_EINVAL / FA_ERANGE / FA_EUNSUPPORTED without
+ *     launching anything; fa_last_error_message() then describes the rejection (thread-local).
+ *   - Values that live in device memory (block ids, slots, context lengths) are bounds-checked
+ *     inside the kernels. A bad value is never dereferenced: the kernel skips the access and
+ *     sets a bit in a per-device status word that fa_device_status() reads back.
+ *   - KV layout per layer (north star): K and V slabs of shape
+ *         [num_blocks, num_kv_heads, block_size, head_dim]
+ *     so one (block, kv_head) page is one contiguous run of block_size*head_dim elements.
+ *     The reference slab is (kv_heads, num_slots, head_dim) with slot = block*bs + offset
+ *     (src/models/common/paged.rs:124-160); element (blk,h,t,:) here is element
+ *     (h, blk*bs+t, :) there.
+ *   - Queries and outputs are packed token-major: [total_tokens, num_heads, head_dim].
+ *   - Query head h reads KV head h / n_rep (src/backend/cpu.rs:5-13).
+ *   - Causal rule (src/backend/cpu.rs:66-68,87-94): a sequence with context length L (all KV
+ *     tokens, cached prefix included) and q_len new query tokens lets query i see KV position j
+ *     iff j <= L - q_len + i.
+ *   - The output dtype equals the query dtype, which must equal the pool dtype
+ *     (src/backend/cpu.rs:109-111).
+ */
+#ifndef FLOUR_ATTN_H
+#define FLOUR_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st *fa_stream_t;
+
+typedef enum fa_status {
+  FA_OK = 0,
+  FA_EINVAL = -1,        /* bad argument (null pointer, shape mismatch, n_rep mismatch ...) */
+  FA_ERANGE = -2,        /* a size or index is out of range (block id, workspace too small) */
+  FA_ECUDA = -3,         /* a CUDA runtime call or kernel launch failed */
+  FA_ETIMEOUT = -4,      /* a bounded device-side wait gave up (see FA_DEVERR_TIMEOUT) */
+  FA_EUNSUPPORTED = -5,  /* valid request this build has no kernel for */
+  FA_EDEVICE = -6        /* a kernel reported bad device-resident data (see FA_DEVERR_*) */
+} fa_status;
+
+typedef enum fa_dtype { FA_F32 = 0, FA_BF16 = 1, FA_F16 = 2 } fa_dtype;
+
+/* Bits of the per-device status word written by the kernels. */
+#define FA_DEVERR_BLOCK_ID 0x1   /* block table entry outside [0, num_blocks) */
+#define FA_DEVERR_CONTEXT 0x2    /* context_len < q_len, or > max_blocks_per_seq*block_size */
+#define FA_DEVERR_SLOT 0x4       /* slot_mapping entry outside [-1, num_blocks*block_size) */
+#define FA_DEVERR_TIMEOUT 0x8    /* a bounded wait on an mbarrier gave up */
+#define FA_DEVERR_SEQLEN 0x10    /* cu_seqlens_q not non-decreasing or past total_q */
+#define FA_DEVERR_PAIR 0x20      /* copy_blocks pair entry outside [0, num_blocks) */
+
+/* One layer of the paged KV pool. */
+typedef struct fa_kv_layer {
+  void *k_cache;          /* device, [num_blocks, num_kv_heads, block_size, head_dim] */
+  void *v_cache;          /* device, same shape as k_cache */
+  int32_t num_blocks;
+  int32_t num_kv_heads;
+  int32_t block_size;     /* the reference uses 16 (src/models/common/cache.rs:10) */
+  int32_t head_dim;
+  int32_t dtype;          /* fa_dtype */
+} fa_kv_layer;
+
+/* ---- version / errors ---------------------------------------------------------------- */
+
+FA_API int32_t fa_abi_version(void);
+FA_API const char *fa_status_string(int32_t status);
+/* Text of the last host-side rejection on the calling thread ("" if none). */
+FA_API const char *fa_last_error_message(void);
+
+/* Wait for `stream`, then copy the current device's status word (FA_DEVERR_* bits) into
+ * *status_out; clear it when `clear` is non-zero. Returns FA_EDEVICE when any bit is set. */
+FA_API fa_status fa_device_status(int32_t *status_out, int32_t clear, fa_stream_t stream);
+
+/* ---- block writes: PagedKvPool::write (src/models/common/paged.rs:186-204) ------------ */
+
+/* reshape_and_cache: scatter num_tokens new K/V rows into their pool slots.
+ *   key[t*key_stride_token + h*key_stride_head + x]   (same for value; strides in elements)
+ *   slot_mapping[t] (device int32): slot = block*block_size + offset, or -1 to skip the token.
+ * Replaces PagedKvPool::write + KvCache::write_current (src/models/common/cache.rs:71-77) and
+ * BlockTable::slots (src/models/common/paged.rs:114-121): slot ids are the reference's.
+ * The reference's (1,Hkv,n,d) tensor is key_stride_token=d, key_stride_head=n*d.
+ * Tokens that map to the same slot: the last one in token order is not guaranteed to win;
+ * callers (like the reference) never map two live tokens to one slot. */
+FA_API fa_status fa_reshape_and_cache(const fa_kv_layer *layer, const void *key, const void *value,
+                               int64_t key_stride_token, int64_t key_stride_head,
+                               int64_t value_stride_token, int64_t value_stride_head,
+                               const int32_t *slot_mapping, int32_t num_tokens,
+                               fa_stream_t stream);
+
+/* ---- block copies: write_block / block_view (src/models/common/paged.rs:211-240,266-279) */
+
+/* Copy whole blocks src -> dst in every layer, K and V (prefix-cache copy-on-write).
+ *   block_mapping: device int32 [num_pairs][2] = (src, dst).
+ * Pairs run concurrently: a dst must not appear twice nor be the src of another pair.
+ * At most FA_MAX_COPY_LAYERS layers per call; all layers must share one shape and dtype. */
+#define FA_MAX_COPY_LAYERS 128
+FA_API fa_status fa_copy_blocks(const fa_kv_layer *layers, int32_t num_layers,
+                         const int32_t *block_mapping, int32_t num_pairs, fa_stream_t stream);
+
+/* PagedKvPool::write_block (paged.rs:211-240): overwrite physical block `block_id` of one layer
+ * with key/value of shape (num_kv_heads, block_size, head_dim) — host or device memory.
+ * Rejects block_id outside [0, num_blocks) with FA_ERANGE. */
+FA_API fa_status fa_write_block(const fa_kv_layer *layer, int32_t block_id, const void *key,
+                         const void *value, fa_stream_t stream);
+
+/* PagedKvPool::block_view (paged.rs:266-279) materialised: copy physical block `block_id` of one
+ * layer into key/value (host or device), shape (num_kv_heads, block_size, head_dim). This is the
+ * per-layer piece of KvCache::export_prefix_bundle (src/models/common/cache.rs:196-213). */
+FA_API fa_status fa_read_block(const fa_kv_layer *layer, int32_t block_id, void *key, void *value,
+                        fa_stream_t stream);
+
+/* ---- paged attention: backend::cpu::paged_attention (src/backend/cpu.rs:57-112) ------- */
+
+/* Bytes of workspace the attention entry points need for these sizes (split-K partials and
+ * merge counters). 0 means no workspace is needed. The workspace must be zero-filled once
+ * before its first use; the kernels leave the counters at zero when they finish. Calls that
+ * run concurrently on different streams need separate workspaces. */
+FA_API size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads,
+                                         int32_t num_kv_heads, int32_t head_dim,
+                                         int32_t max_context_len, int32_t max_seqlen_q);
+
+/* General entry, same contract as paged_attention(q, blocks, n_rep, scale) for a batch of
+ * sequences with varying query counts (decode when every sequence has one query token).
+ *   query/out       device [total_q, num_heads, head_dim], pool dtype
+ *   cu_seqlens_q    device int32 [num_seqs+1], cu_seqlens_q[0]=0, cu_seqlens_q[S]=total_q
+ *   context_lens    device int32 [num_seqs]: KV length L including the new tokens
+ *   block_tables    device int32 [num_seqs, max_blocks_per_seq]: logical -> physical block
+ *                   (the reference's KvCache::gather_blocks, cache.rs:83-96, one table per seq)
+ *   num_heads == n_rep * layer->num_kv_heads, else FA_EINVAL (cpu.rs:78-79 repeat_kv)
+ *   max_seqlen_q / max_context_len: host-side upper bounds used for launch sizing. */
+FA_API fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query, void *out,
+                             const int32_t *cu_seqlens_q, const int32_t *context_lens,
+                             const int32_t *block_tables, int32_t max_blocks_per_seq,
+                             int32_t num_seqs, int32_t num_heads, int32_t n_rep,
+                             int32_t total_q, int32_t max_seqlen_q, int32_t max_context_len,
+                             float scale, void *workspace, size_t workspace_bytes,
+                             fa_stream_t stream);
+
+/* Decode specialisation (one query token per sequence): query/out [num_seqs, num_heads, d].
+ * Split-K over the context with a log-sum-exp merge of the partial results. */
+FA_API fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, void *out,
+                          const int32_t *context_lens, const int32_t *block_tables,
+                          int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
+                          int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
+                          size_t workspace_bytes, fa_stream_t stream);
+
+/* Varlen causal prefill over prefix-cached blocks: the suffix tokens' K/V must already be in
+ * the pool (fa_reshape_and_cache); queries are the suffix tokens only. */
+FA_API fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *out,
+                           const int32_t *cu_seqlens_q, const int32_t *context_lens,
+                           const int32_t *block_tables, int32_t max_blocks_per_seq,
+                           int32_t num_seqs, int32_t num_heads, int32_t n_rep, int32_t total_q,
+                           int32_t max_seqlen_q, int32_t max_context_len, float scale,
+                           void *workspace, size_t workspace_bytes, fa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLOUR_ATTN_H */

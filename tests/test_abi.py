@@ -1,0 +1,103 @@
+"""The C-ABI library loads, exports every declared symbol, and rejects bad arguments on the
+host before touching a GPU (no compute calls here)."""
+
+import ctypes
+import re
+
+import pytest
+
+from flour_b200 import _lib
+from flour_b200._lib import FaKvLayer, lib
+
+
+def declared_functions():
+    text = _lib.HEADER_PATH.read_text()
+    return sorted(set(re.findall(r"FA_API\s+[\w\s\*]*?\b(fa_\w+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    decl = declared_functions()
+    assert decl == sorted(_lib.SIGNATURES), (decl, sorted(_lib.SIGNATURES))
+    assert len(decl) >= 12
+
+
+def test_library_exports_every_declared_symbol():
+    L = lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+
+
+def test_library_is_sm100a_and_has_no_multicast():
+    data = _lib.LIB_PATH.read_bytes()
+    assert b"sm_100a" in data
+    src = (_lib.LIB_PATH.parent / "csrc")
+    for f in src.glob("*.cu*"):
+        assert "multicast::cluster" not in f.read_text(), f
+
+
+def test_status_strings():
+    L = lib()
+    assert L.fa_abi_version() == 1
+    assert L.fa_status_string(0) == b"ok"
+    assert L.fa_status_string(-1) == b"invalid argument"
+    assert L.fa_status_string(-6) == b"kernel reported bad device data"
+
+
+def layer(nb=8, kvh=2, bs=16, d=64, dt=_lib.FA_BF16, k=0x1000, v=0x2000):
+    return FaKvLayer(k, v, nb, kvh, bs, d, dt)
+
+
+def test_host_validation_rejects_before_launch():
+    L = lib()
+    P = ctypes.c_void_p
+    ly = layer()
+    fake = P(0x10000)
+    # NULL layer
+    assert L.fa_paged_decode(None, fake, fake, fake, fake, 4, 1, 4, 2, 16, 0.1, None, 0, None) == _lib.FA_EINVAL
+    assert b"layer is NULL" in L.fa_last_error_message()
+    # num_heads != n_rep * kv_heads (repeat_kv contract, cpu.rs:78-79)
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 5, 2, 16, 0.1, None, 0, None) == _lib.FA_EINVAL
+    assert b"n_rep" in L.fa_last_error_message()
+    # context longer than the table can hold
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 65, 0.1, None, 0, None) == _lib.FA_ERANGE
+    # non-finite scale
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 16, float("nan"), None, 0, None) == _lib.FA_EINVAL
+    # bad dtype
+    bad = layer(dt=7)
+    assert L.fa_reshape_and_cache(ctypes.byref(bad), fake, fake, 128, 64, 128, 64, fake, 3, None) == _lib.FA_EINVAL
+    # write_block / read_block out of range (PagedKvPool rejects bad blocks)
+    assert L.fa_write_block(ctypes.byref(ly), 8, fake, fake, None) == _lib.FA_ERANGE
+    assert L.fa_read_block(ctypes.byref(ly), -1, fake, fake, None) == _lib.FA_ERANGE
+    # copy_blocks layer-count bounds and shape agreement
+    assert L.fa_copy_blocks(ctypes.byref(ly), 0, fake, 1, None) == _lib.FA_EINVAL
+    two = (FaKvLayer * 2)(layer(), layer(d=128))
+    assert L.fa_copy_blocks(two, 2, fake, 1, None) == _lib.FA_EINVAL
+    # prefill: query longer than the context
+    assert L.fa_paged_prefill(ctypes.byref(ly), fake, fake, fake, fake, fake, 4, 1, 4, 2, 8, 8, 4, 0.1, None, 0, None) == _lib.FA_ERANGE
+    # empty work is a no-op success
+    assert L.fa_reshape_and_cache(ctypes.byref(ly), fake, fake, 128, 64, 128, 64, fake, 0, None) == _lib.FA_OK
+    assert L.fa_copy_blocks(ctypes.byref(ly), 1, fake, 0, None) == _lib.FA_OK
+
+
+def test_workspace_sizes():
+    L = lib()
+    # Prefill needs no workspace; short decode contexts fit in one split.
+    assert L.fa_paged_attention_workspace_size(16, 32, 8, 128, 2048, 2048) == 0
+    # C2 decode: 64 sequences x 8 kv heads, contexts up to 4096 -> split-K partials.
+    ws = L.fa_paged_attention_workspace_size(64, 32, 8, 128, 4096, 1)
+    assert ws > 64 * 32 * 128 * 4
+    # C4 long context needs more splits -> a larger workspace.
+    assert L.fa_paged_attention_workspace_size(16, 32, 8, 128, 32768, 1) > 16 * 32 * 128 * 4 * 4
+    assert L.fa_paged_attention_workspace_size(0, 32, 8, 128, 4096, 1) == 0
+
+
+def test_decode_workspace_too_small_is_rejected_without_launch():
+    L = lib()
+    ly = layer(nb=4096, kvh=8, bs=16, d=128)
+    fake = ctypes.c_void_p(0x10000)
+    need = L.fa_paged_attention_workspace_size(64, 32, 8, 128, 4096, 1)
+    assert need > 0
+    st = L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 256, 64, 32, 4, 4096, 0.1,
+                           ctypes.c_void_p(0x100000), need - 1, None)
+    assert st == _lib.FA_ERANGE
+    assert b"workspace" in L.fa_last_error_message()

@@ -1,0 +1,94 @@
+"""Host-side mirror of the reference interface (no GPU): ports of the allocator / block table
+tests (src/models/common/paged.rs:343-411) and the batch metadata builder."""
+
+import numpy as np
+import pytest
+import torch
+
+from flour_b200.paged import BlockAllocator, BlockTable, build_batch
+from flour_b200.workloads import lpt_partition, make_c3, c5_contexts
+
+
+def test_allocator_hands_out_distinct_blocks_then_exhausts():  # paged.rs:343-353
+    alloc = BlockAllocator(2)
+    assert alloc.num_free() == 2
+    a, b = alloc.allocate(), alloc.allocate()
+    assert a != b
+    assert alloc.allocate() is None
+    assert alloc.decref(a)
+    assert alloc.num_free() == 1
+    assert alloc.allocate() == a
+
+
+def test_allocator_refcounts_govern_when_a_block_is_freed():  # paged.rs:355-375
+    alloc = BlockAllocator(2)
+    a = alloc.allocate()
+    assert a == 0 and alloc.ref_count(a) == 1  # first allocation is block 0 (paged.rs:14)
+    alloc.incref(a)
+    assert alloc.ref_count(a) == 2
+    assert not alloc.decref(a)
+    assert alloc.num_free() == 1
+    assert alloc.decref(a)
+    assert alloc.ref_count(a) == 0 and alloc.num_free() == 2
+    assert alloc.allocate() == a
+
+
+def test_block_table_maps_logical_positions_to_physical_slots():  # paged.rs:377-394
+    t = BlockTable(2)
+    assert t.is_empty()
+    t.push_block(5)
+    t.push_block(3)
+    assert t.capacity() == 4
+    assert [t.slot(p) for p in range(4)] == [10, 11, 6, 7]
+    t.advance(3)
+    assert t.len() == 3
+    assert t.slots(0, 3) == [10, 11, 6]
+
+
+def test_block_table_exposes_blocks_and_clears():  # paged.rs:396-411
+    t = BlockTable(2)
+    t.push_block(5)
+    t.push_block(3)
+    t.advance(4)
+    assert t.blocks() == [5, 3] and t.block_at(0) == 5 and t.block_at(1) == 3
+    t.clear()
+    assert t.is_empty() and t.len() == 0 and t.blocks() == [] and t.block_size() == 2
+
+
+def test_build_batch_matches_per_sequence_slots():
+    tables = []
+    for blocks, n in (([4, 9], 20), ([1], 3), ([7, 2, 5], 40)):
+        t = BlockTable(16)
+        for b in blocks:
+            t.push_block(b)
+        t.advance(n)
+        tables.append(t)
+    meta = build_batch(tables, [1, 3, 8], "cpu")
+    assert meta.block_tables.tolist() == [[4, 9, 0], [1, 0, 0], [7, 2, 5]]
+    assert meta.context_lens.tolist() == [20, 3, 40]
+    assert meta.cu_seqlens_q.tolist() == [0, 1, 4, 12]
+    want = tables[0].slots(19, 20) + tables[1].slots(0, 3) + tables[2].slots(32, 40)
+    assert meta.slot_mapping.tolist() == want
+    assert meta.max_context_len == 40 and meta.max_seqlen_q == 8
+
+
+def test_lpt_partition_balances_lognormal_contexts():
+    ctx = c5_contexts(5)
+    parts = lpt_partition(ctx, 8)
+    assert sorted(i for p in parts for i in p) == list(range(len(ctx)))
+    loads = [ctx[p].sum() for p in parts]
+    assert max(loads) / min(loads) < 1.02
+
+
+def test_c3_generator_shares_prefix_blocks():
+    b = make_c3("cpu", seed=3)
+    bt = b.block_tables.numpy()
+    for g0 in range(0, 16, 4):
+        p = int(b.prefix[g0]) // 16
+        for i in range(g0 + 1, g0 + 4):
+            assert (bt[i, :p] == bt[g0, :p]).all()
+        assert b.prefix[g0] % 16 == 0 and b.prefix[g0] <= 0.5 * b.lens[g0:g0 + 4].min()
+    # every suffix slot is unique and lies outside the shared prefixes
+    s = b.slot_mapping.numpy()
+    assert len(np.unique(s)) == len(s)
+    assert b.flops() > 0
