@@ -46,7 +46,7 @@ BATCH = 64
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1000)
@@ -78,7 +78,7 @@ def profile_traffic(name: str):
 class ClockSampler:
     """nvidia-smi samples every 200 ms while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -86,6 +86,10 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.file = None
+        self.window = None  # (t0, t1) host wall-clock bounds of the timed region
+
+    def mark(self, t0: float, t1: float) -> None:
+        self.window = (t0, t1)
 
     def __enter__(self):
         try:
@@ -116,12 +120,15 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             try:
-                sm.append(float(r[1]))
-                smax.append(float(r[2]))
-                power.append(float(r[3]))
+                ts = time.mktime(time.strptime(r[0].strip().split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                if self.window and not (self.window[0] - 1.0 <= ts <= self.window[1] + 1.0):
+                    continue
+                sm.append(float(r[2]))
+                smax.append(float(r[3]))
+                power.append(float(r[4]))
             except (ValueError, IndexError):
                 continue
-            for n, v in zip(names, r[5:9]):
+            for n, v in zip(names, r[6:10]):
                 if v.strip().lower() == "active":
                     reasons.add(n)
         load = [s for s, p in zip(sm, power) if p > 200.0] or sm
@@ -272,13 +279,20 @@ def run_ours(args):
     # ---- timed region: K graph replays of the 32-layer decode step ----------------------
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        # Pre-roll (untimed) so the sampler is up and the GPU is under load when timing starts.
+        t_end = time.time() + 0.6
+        while time.time() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
+        w0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):
             graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
+        clocks.mark(w0, time.time())
         barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
     ms_per_step = ms / args.steps
