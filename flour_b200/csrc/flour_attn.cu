@@ -11,6 +11,7 @@
 #include "attn_generic.cuh"
 #include "cache_ops.cuh"
 #include "decode_sm100.cuh"
+#include "prefill_sm100.cuh"
 #include "flour_attn.h"
 
 namespace {
@@ -84,6 +85,25 @@ fa_status make_page_map(CUtensorMap *map, void *base, int64_t rows, int head_dim
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FA_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return FA_OK;
+}
+
+// 3-D map over packed queries [total_q, num_heads, 128] for the prefill kernel: one box is the
+// n_rep heads of one KV group for tq consecutive tokens, 64 values of head_dim wide.
+fa_status make_q_map(CUtensorMap *map, const void *q, int total_q, int num_heads, int n_rep, int tq,
+                     int32_t dt) {
+  if (fa_status s = get_encoder(); s != FA_OK) return s;
+  const CUtensorMapDataType t =
+      dt == FA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {128, cuuint64_t(num_heads), cuuint64_t(total_q)};
+  cuuint64_t strides[2] = {256, cuuint64_t(num_heads) * 256};
+  cuuint32_t box[3] = {64, cuuint32_t(n_rep), cuuint32_t(tq)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, t, 3, const_cast<void *>(q), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ECUDA, "cuTensorMapEncodeTiled (queries) failed (%d)", int(r));
   return FA_OK;
 }
 
@@ -233,6 +253,55 @@ fa_status launch_generic(const fa_kv_layer *L, const void *q, void *out, const i
     default: fa::generic_attn_kernel<__half><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
   }
   return check_launch("paged_attention (generic)");
+}
+
+bool prefill_fast_path(const fa_kv_layer *L, int n_rep, int total_q, const void *q, const void *out) {
+  return (L->dtype == FA_BF16 || L->dtype == FA_F16) && L->block_size == fa::kPage &&
+         L->head_dim == 128 && n_rep >= 1 && n_rep <= 128 && total_q >= 128 &&
+         L->num_kv_heads <= 65535 &&
+         int64_t(L->num_blocks) * L->num_kv_heads * L->block_size < (int64_t(1) << 31) &&
+         aligned(L->k_cache, 16) && aligned(L->v_cache, 16) && aligned(q, 16) && aligned(out, 16);
+}
+
+template <typename T>
+fa_status launch_prefill_t(const fa::PrefillParams &p, const CUtensorMap &tq, const CUtensorMap &tk,
+                           const CUtensorMap &tv, int grid_x, cudaStream_t stream) {
+  using S = fa::PrefillSmem;
+  auto kern = fa::paged_prefill_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "prefill: set smem attribute: %s", cudaGetErrorString(e));
+  kern<<<dim3(grid_x, p.num_kv_heads), fa::kPfThreads, S::kAlloc, stream>>>(p, tq, tk, tv);
+  return check_launch("paged_prefill");
+}
+
+fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const int32_t *cu,
+                         const int32_t *ctx, const int32_t *tables, int max_blocks, int num_seqs,
+                         int num_heads, int n_rep, int total_q, float scale, cudaStream_t stream) {
+  fa::PrefillParams p{};
+  p.out = out;
+  p.cu_seqlens_q = cu;
+  p.context_lens = ctx;
+  p.block_tables = tables;
+  p.max_blocks_per_seq = max_blocks;
+  p.num_seqs = num_seqs;
+  p.num_heads = num_heads;
+  p.num_kv_heads = L->num_kv_heads;
+  p.n_rep = n_rep;
+  p.num_blocks = L->num_blocks;
+  p.total_q = total_q;
+  p.tq = 128 / n_rep;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t rows = int64_t(L->num_blocks) * L->num_kv_heads * L->block_size;
+  CUtensorMap tmq, tk, tv;
+  if (fa_status s = make_q_map(&tmq, q, total_q, num_heads, n_rep, p.tq, L->dtype); s != FA_OK) return s;
+  if (fa_status s = make_page_map(&tk, L->k_cache, rows, 128, L->dtype); s != FA_OK) return s;
+  if (fa_status s = make_page_map(&tv, L->v_cache, rows, 128, L->dtype); s != FA_OK) return s;
+  // Upper bound on the number of (sequence, chunk) work items; extra CTAs exit at once.
+  const int64_t chunk = 2 * p.tq;
+  const int64_t grid_x = (total_q + chunk - 1) / chunk + num_seqs;
+  if (grid_x > 0x7fffffff) return fail(FA_EUNSUPPORTED, "prefill: too many query tokens");
+  if (L->dtype == FA_BF16) return launch_prefill_t<__nv_bfloat16>(p, tmq, tk, tv, int(grid_x), stream);
+  return launch_prefill_t<__half>(p, tmq, tk, tv, int(grid_x), stream);
 }
 
 fa_status check_attention_args(const char *who, const fa_kv_layer *L, const void *q, const void *out,
@@ -466,6 +535,9 @@ fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *ou
   (void)workspace;
   (void)workspace_bytes;
   if (total_q == 0 || num_seqs == 0) return ok();
+  if (prefill_fast_path(layer, n_rep, total_q, query, out))
+    return launch_prefill(layer, query, out, cu_seqlens_q, context_lens, block_tables,
+                          max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, stream);
   return launch_generic(layer, query, out, cu_seqlens_q, context_lens, block_tables,
                         max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, stream);
 }

@@ -1,0 +1,114 @@
+"""The tcgen05 varlen prefill kernel (bf16/f16, head_dim 128, block_size 16) against the oracle
+(src/backend/cpu.rs:57-112), max-abs 2e-2, across GQA ratios, chunk boundaries, empty and
+one-token sequences, long cached prefixes and the full C3 configuration."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from flour_b200 import _lib, ops
+from flour_b200.workloads import LLAMA8B, QWEN7B, Heads, PrefillBatch, make_c3
+
+from _util import f32, max_abs, oracle_attention
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def build(device, heads, lens, prefix, seed, dtype=torch.bfloat16):
+    """Explicit per-sequence (length, prefix) batch; prefix blocks private per sequence."""
+    rng = np.random.default_rng(seed)
+    bs = heads.block_size
+    lens = np.asarray(lens, dtype=np.int64)
+    prefix = np.asarray(prefix, dtype=np.int64)
+    pages = (lens + bs - 1) // bs
+    total = int(pages.sum()) + 3
+    perm = rng.permutation(total).astype(np.int32)
+    bt = np.zeros((len(lens), max(1, int(pages.max()))), dtype=np.int32)
+    o = 0
+    for i, n in enumerate(pages):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    suffix = lens - prefix
+    cu = np.concatenate([[0], np.cumsum(suffix)]).astype(np.int32)
+    slots = [int(bt[i, pos // bs]) * bs + pos % bs for i in range(len(lens))
+             for pos in range(int(prefix[i]), int(lens[i]))]
+    g = torch.Generator(device=device).manual_seed(seed)
+    shape = (total, heads.num_kv_heads, bs, heads.head_dim)
+    kc = torch.randn(shape, device=device, generator=g).to(dtype)
+    vc = torch.randn(shape, device=device, generator=g).to(dtype)
+    tq = int(cu[-1])
+    q = torch.randn((tq, heads.num_heads, heads.head_dim), device=device, generator=g).to(dtype)
+    key = torch.randn((tq, heads.num_kv_heads, heads.head_dim), device=device, generator=g).to(dtype)
+    val = torch.randn((tq, heads.num_kv_heads, heads.head_dim), device=device, generator=g).to(dtype)
+    return PrefillBatch(heads, dtype, q, key, val, [kc], [vc], torch.from_numpy(cu).to(device),
+                        torch.from_numpy(lens.astype(np.int32)).to(device),
+                        torch.from_numpy(bt).to(device),
+                        torch.tensor(slots, dtype=torch.int32, device=device), lens, prefix,
+                        int(suffix.max()), int(lens.max()), total)
+
+
+def run_and_check(b, tol=TOL):
+    h = b.heads
+    scale = 1 / math.sqrt(h.head_dim)
+    ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
+    out = ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                            b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len,
+                            ops.Workspace(b.q.device))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    want = oracle_attention(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                            b.block_tables, h.n_rep, scale)
+    err = max_abs(f32(out), want)
+    assert err <= tol, f"max-abs {err}"
+    return out
+
+
+def test_single_sequence_no_prefix(device):
+    run_and_check(build(device, LLAMA8B, [300], [0], 1))
+
+
+def test_chunk_boundaries(device):
+    # lengths around multiples of the 64-token chunk and the 128-token KV tile
+    run_and_check(build(device, LLAMA8B, [63, 64, 65, 127, 128, 129, 200], [0] * 7, 2))
+
+
+def test_long_prefix_short_suffix(device):
+    run_and_check(build(device, LLAMA8B, [1500, 900, 400], [1472, 640, 16], 3))
+
+
+def test_empty_and_one_token_sequences(device):
+    run_and_check(build(device, LLAMA8B, [40, 200, 77, 130, 90], [40, 199, 0, 64, 89], 4))
+
+
+@pytest.mark.parametrize("heads", [Heads(8, 8, 128), Heads(32, 4, 128), QWEN7B, Heads(16, 2, 128)])
+def test_gqa_ratios(device, heads):
+    run_and_check(build(device, heads, [260, 131, 75], [32, 0, 48], 5))
+
+
+def test_f16_pool(device):
+    run_and_check(build(device, LLAMA8B, [333, 150], [96, 0], 6, dtype=torch.float16))
+
+
+def test_c3_full_configuration(device):
+    run_and_check(make_c3(device, seed=1003))
+
+
+def test_prefill_repeatable(device):
+    b = build(device, LLAMA8B, [700, 500], [128, 0], 7)
+    o1 = run_and_check(b).clone()
+    o2 = run_and_check(b)
+    assert torch.equal(o1, o2)
+
+
+def test_bad_block_id_reported(device):
+    b = build(device, LLAMA8B, [300, 200], [0, 0], 8)
+    ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
+    bt = b.block_tables.clone()
+    bt[1, 2] = 1 << 20
+    ops.device_status()
+    ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens, bt, 4,
+                      1 / math.sqrt(128), b.max_seqlen_q, b.max_context_len)
+    assert ops.device_status() & _lib.FA_DEVERR_BLOCK_ID
