@@ -214,8 +214,8 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
-    import flour_b200  # noqa: F401  (loads libflour_attn.so, fails loudly without it)
-    from flour_b200 import ops
+    from flour_b200 import _lib, ops
+    _lib.lib()  # loads libflour_attn.so; raises without it (no fallback path exists)
     from flour_b200.workloads import LLAMA8B, c2_contexts, make_c3, make_decode
 
     hbm_peak, tc_peak, tc_sustained, peak_kind = peaks()

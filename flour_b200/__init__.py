@@ -2,13 +2,12 @@
 
 The compute lives in ``libflour_attn.so`` (CUDA, C ABI in ``include/flour_attn.h``); this
 package only binds it (``_lib``), wraps it for torch tensors (``ops``) and mirrors the reference's
-host interface (``paged``). Importing it loads the library and fails if it is missing.
+host interface (``paged``). The library is loaded on first use; every entry point raises if it
+is missing or stale — there is no fallback implementation.
 """
 
 from . import _lib
 from ._lib import FlourAttnError
-
-_lib.lib()  # fail loudly at import when the CUDA library is absent
 
 from . import ops, paged  # noqa: E402
 
