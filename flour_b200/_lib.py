@@ -21,6 +21,7 @@ FA_DEVERR_TIMEOUT = 0x8
 FA_DEVERR_SEQLEN = 0x10
 FA_DEVERR_PAIR = 0x20
 FA_MAX_COPY_LAYERS = 128
+FA_NOALLOC_DECODE_SCRATCH_BYTES = 8 * 1024 * 1024
 
 # Every function the header declares, with its ctypes signature.
 _P, _I32, _I64, _SZ, _F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float
@@ -55,6 +56,7 @@ SIGNATURES = {
     "fa_paged_attention": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                   _I32, _F, _P, _SZ, _P]),
     "fa_paged_decode": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P, _SZ, _P]),
+    "fa_paged_decode_noalloc": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P]),
     "fa_paged_prefill": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                                 _F, _P, _SZ, _P]),
 }

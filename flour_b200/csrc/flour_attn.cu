@@ -321,6 +321,34 @@ fa_status check_attention_args(const char *who, const fa_kv_layer *L, const void
   return FA_OK;
 }
 
+// ---- decode scratch for callers that cannot allocate ------------------------------------
+
+// Split-K partials and merge tickets of fa_paged_decode_noalloc. Host code must not pass this
+// symbol to a kernel (on the host it names a stand-in, not device memory): its device address
+// comes from cudaGetSymbolAddress, looked up once per device with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FA_NOALLOC_DECODE_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+fa_status noalloc_scratch(void **out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "paged_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(FA_EUNSUPPORTED, "paged_decode_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(FA_ECUDA, "paged_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -557,6 +585,47 @@ fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query, void *
   return fa_paged_prefill(layer, query, out, cu_seqlens_q, context_lens, block_tables,
                           max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, max_seqlen_q,
                           max_context_len, scale, workspace, workspace_bytes, stream);
+}
+
+fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, void *out,
+                                  const int32_t *context_lens, const int32_t *block_tables,
+                                  int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
+                                  int32_t n_rep, int32_t max_context_len, float scale,
+                                  fa_stream_t stream) {
+  if (fa_status s = check_attention_args("paged_decode_noalloc", layer, query, out, context_lens,
+                                         block_tables, max_blocks_per_seq, num_seqs, num_heads,
+                                         n_rep, max_context_len, scale);
+      s != FA_OK)
+    return s;
+  if (num_seqs == 0) return ok();
+  if (max_context_len < 1) return fail(FA_ERANGE, "paged_decode_noalloc: max_context_len must be >= 1");
+  if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "paged_decode_noalloc: more than 65535 sequences per call");
+  if (!decode_fast_path(layer, n_rep, query, out))  // the generic kernel uses no scratch
+    return launch_generic(layer, query, out, nullptr, context_lens, block_tables,
+                          max_blocks_per_seq, num_seqs, num_heads, n_rep, num_seqs, scale, stream);
+  DecodePlan plan;
+  if (!plan_decode(num_seqs, layer->num_kv_heads, max_context_len, &plan))
+    return fail(FA_EUNSUPPORTED, "paged_decode_noalloc: context of %d tokens needs more than %d splits",
+                max_context_len, fa::kDecodeMaxSplits);
+  const DecodeWorkspace w =
+      decode_workspace_layout(num_seqs, num_heads, layer->num_kv_heads, layer->head_dim, plan);
+  if (w.bytes > FA_NOALLOC_DECODE_SCRATCH_BYTES)
+    return fail(FA_ERANGE,
+                "paged_decode_noalloc: %zu bytes of split-K scratch needed, the built-in buffer "
+                "holds %u; call fa_paged_decode with a workspace instead",
+                w.bytes, FA_NOALLOC_DECODE_SCRATCH_BYTES);
+  void *scratch = nullptr;
+  if (fa_status s = noalloc_scratch(&scratch); s != FA_OK) return s;
+  if (w.bytes > 0) {
+    // The merge tickets must start at zero; the previous call's contents are still there.
+    const cudaError_t e = cudaMemsetAsync(static_cast<char *>(scratch) + w.counters_off, 0,
+                                          size_t(num_seqs) * layer->num_kv_heads * sizeof(int32_t),
+                                          stream);
+    if (e != cudaSuccess) return fail(FA_ECUDA, "paged_decode_noalloc: %s", cudaGetErrorString(e));
+  }
+  return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq, num_seqs,
+                       num_heads, n_rep, max_context_len, scale, scratch,
+                       FA_NOALLOC_DECODE_SCRATCH_BYTES, stream);
 }
 
 }  // extern "C"

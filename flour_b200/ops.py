@@ -138,6 +138,21 @@ def paged_decode(query, k_cache, v_cache, block_tables, context_lens, n_rep: int
     return out
 
 
+def paged_decode_noalloc(query, k_cache, v_cache, block_tables, context_lens, n_rep: int,
+                        scale: float, max_context_len: int, out=None, stream=None):
+    """paged_decode without a workspace: the split-K scratch is the library's fixed buffer
+    (fa_paged_decode_noalloc). Calls on different streams must not overlap on the GPU."""
+    layer = layer_desc(k_cache, v_cache)
+    query = query.contiguous()
+    out = torch.empty_like(query) if out is None else out
+    bt, cl = _i32(block_tables, "block_tables"), _i32(context_lens, "context_lens")
+    B, hq, d = query.shape
+    check(lib().fa_paged_decode_noalloc(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cl),
+                                        _ptr(bt), bt.shape[1], B, hq, n_rep, max_context_len,
+                                        scale, _stream(stream)), "paged_decode_noalloc")
+    return out
+
+
 def paged_prefill(query, k_cache, v_cache, cu_seqlens_q, context_lens, block_tables, n_rep: int,
                   scale: float, max_seqlen_q: int, max_context_len: int,
                   workspace: Workspace | None = None, out=None, stream=None):

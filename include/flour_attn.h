@@ -168,6 +168,28 @@ FA_API fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, vo
                           int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
                           size_t workspace_bytes, fa_stream_t stream);
 
+/* Decode without a caller-provided workspace. No counterpart in the reference: the reference's
+ * CPU path never needs scratch memory. Some callers of this library cannot allocate device
+ * memory at the point where they run attention — for example an engine whose KV pool was sized
+ * to fill the GPU's memory and that forbids allocations while serving, or a host runtime that
+ * reaches the GPU only through these raw-pointer entry points and has no device allocator of
+ * its own. For them this variant takes its split-K scratch from a fixed buffer inside the
+ * library (FA_NOALLOC_DECODE_SCRATCH_BYTES; every GPU that loads the library holds it until the
+ * process exits) and calls no allocating routine. Same arguments and results as
+ * fa_paged_decode minus the workspace.
+ *   - Requests whose split-K scratch would exceed FA_NOALLOC_DECODE_SCRATCH_BYTES are rejected
+ *     with FA_ERANGE (use fa_paged_decode with a workspace for those).
+ *   - The first call on each device looks up the buffer's device address (with that device
+ *     current); make that first call before any stream capture.
+ *   - All calls share the one buffer per device, so calls whose GPU work overlaps (different
+ *     streams, or threads without ordering) race; order them on one stream. */
+#define FA_NOALLOC_DECODE_SCRATCH_BYTES (8u * 1024u * 1024u)
+FA_API fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, void *out,
+                                         const int32_t *context_lens, const int32_t *block_tables,
+                                         int32_t max_blocks_per_seq, int32_t num_seqs,
+                                         int32_t num_heads, int32_t n_rep, int32_t max_context_len,
+                                         float scale, fa_stream_t stream);
+
 /* Varlen causal prefill over prefix-cached blocks: the suffix tokens' K/V must already be in
  * the pool (fa_reshape_and_cache); queries are the suffix tokens only. */
 FA_API fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *out,
