@@ -255,12 +255,29 @@ fa_status launch_generic(const fa_kv_layer *L, const void *q, void *out, const i
   return check_launch("paged_attention (generic)");
 }
 
-bool prefill_fast_path(const fa_kv_layer *L, int n_rep, int total_q, const void *q, const void *out) {
+bool prefill_fast_path(const fa_kv_layer *L, int n_rep, int total_q, float scale, const void *q,
+                       const void *out) {
   return (L->dtype == FA_BF16 || L->dtype == FA_F16) && L->block_size == fa::kPage &&
-         L->head_dim == 128 && n_rep >= 1 && n_rep <= 128 && total_q >= 128 &&
-         L->num_kv_heads <= 65535 &&
+         L->head_dim == 128 && n_rep >= 1 && n_rep <= 128 && total_q >= 128 && scale > 0.f &&
          int64_t(L->num_blocks) * L->num_kv_heads * L->block_size < (int64_t(1) << 31) &&
          aligned(L->k_cache, 16) && aligned(L->v_cache, 16) && aligned(q, 16) && aligned(out, 16);
+}
+
+// Bytes of workspace the prefill kernel needs: two work counters (zero-filled once by the caller,
+// returned to zero by the kernel).
+constexpr size_t kPrefillWorkspace = 256;
+
+int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kSmCount;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = kSmCount;
+    cached[dev] = n;
+  }
+  return cached[dev];
 }
 
 template <typename T>
@@ -270,20 +287,22 @@ fa_status launch_prefill_t(const fa::PrefillParams &p, const CUtensorMap &tq, co
   auto kern = fa::paged_prefill_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "prefill: set smem attribute: %s", cudaGetErrorString(e));
-  kern<<<dim3(grid_x, p.num_kv_heads), fa::kPfThreads, S::kAlloc, stream>>>(p, tq, tk, tv);
+  kern<<<grid_x, fa::kPfThreads, S::kAlloc, stream>>>(p, tq, tk, tv);
   return check_launch("paged_prefill");
 }
 
 fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const int32_t *cu,
                          const int32_t *ctx, const int32_t *tables, int max_blocks, int num_seqs,
-                         int num_heads, int n_rep, int total_q, float scale, cudaStream_t stream) {
+                         int num_heads, int n_rep, int total_q, float scale, void *ws,
+                         size_t ws_bytes, cudaStream_t stream) {
+  if (!ws) return fail(FA_EINVAL, "prefill: workspace is NULL but %zu bytes are needed", kPrefillWorkspace);
+  if (ws_bytes < kPrefillWorkspace)
+    return fail(FA_ERANGE, "prefill: workspace of %zu bytes, %zu needed", ws_bytes, kPrefillWorkspace);
+  if (!aligned(ws, 256)) return fail(FA_EINVAL, "prefill: workspace must be 256-byte aligned");
   fa::PrefillParams p{};
   p.out = out;
-  p.cu_seqlens_q = cu;
-  p.context_lens = ctx;
-  p.block_tables = tables;
+  p.counters = static_cast<int32_t *>(ws);
   p.max_blocks_per_seq = max_blocks;
-  p.num_seqs = num_seqs;
   p.num_heads = num_heads;
   p.num_kv_heads = L->num_kv_heads;
   p.n_rep = n_rep;
@@ -296,12 +315,21 @@ fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const i
   if (fa_status s = make_q_map(&tmq, q, total_q, num_heads, n_rep, p.tq, L->dtype); s != FA_OK) return s;
   if (fa_status s = make_page_map(&tk, L->k_cache, rows, 128, L->dtype); s != FA_OK) return s;
   if (fa_status s = make_page_map(&tv, L->v_cache, rows, 128, L->dtype); s != FA_OK) return s;
-  // Upper bound on the number of (sequence, chunk) work items; extra CTAs exit at once.
+  // One persistent CTA per SM; at most kPfMaxSeqs sequences per launch (their chunk table lives
+  // in shared memory), larger batches run as consecutive launches on the same stream.
   const int64_t chunk = 2 * p.tq;
-  const int64_t grid_x = (total_q + chunk - 1) / chunk + num_seqs;
-  if (grid_x > 0x7fffffff) return fail(FA_EUNSUPPORTED, "prefill: too many query tokens");
-  if (L->dtype == FA_BF16) return launch_prefill_t<__nv_bfloat16>(p, tmq, tk, tv, int(grid_x), stream);
-  return launch_prefill_t<__half>(p, tmq, tk, tv, int(grid_x), stream);
+  for (int s0 = 0; s0 < num_seqs; s0 += fa::kPfMaxSeqs) {
+    p.num_seqs = std::min(fa::kPfMaxSeqs, num_seqs - s0);
+    p.cu_seqlens_q = cu + s0;
+    p.context_lens = ctx + s0;
+    p.block_tables = tables + size_t(s0) * max_blocks;
+    const int64_t items = ((int64_t(total_q) + chunk - 1) / chunk + p.num_seqs) * L->num_kv_heads;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>(sm_count(), items)));
+    fa_status st = L->dtype == FA_BF16 ? launch_prefill_t<__nv_bfloat16>(p, tmq, tk, tv, grid, stream)
+                                       : launch_prefill_t<__half>(p, tmq, tk, tv, grid, stream);
+    if (st != FA_OK) return st;
+  }
+  return ok();
 }
 
 fa_status check_attention_args(const char *who, const fa_kv_layer *L, const void *q, const void *out,
@@ -518,7 +546,7 @@ size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads, in
                                          int32_t max_seqlen_q) {
   if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_context_len <= 0)
     return 0;
-  if (max_seqlen_q != 1) return 0;
+  if (max_seqlen_q != 1) return kPrefillWorkspace;
   DecodePlan plan;
   if (!plan_decode(num_seqs, num_kv_heads, max_context_len, &plan)) return 0;
   return decode_workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, plan).bytes;
@@ -560,12 +588,11 @@ fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *ou
   if (total_q < 0 || max_seqlen_q < 0) return fail(FA_EINVAL, "paged_prefill: negative total_q/max_seqlen_q");
   if (max_seqlen_q > max_context_len)
     return fail(FA_ERANGE, "paged_prefill: max_seqlen_q %d > max_context_len %d", max_seqlen_q, max_context_len);
-  (void)workspace;
-  (void)workspace_bytes;
   if (total_q == 0 || num_seqs == 0) return ok();
-  if (prefill_fast_path(layer, n_rep, total_q, query, out))
+  if (prefill_fast_path(layer, n_rep, total_q, scale, query, out))
     return launch_prefill(layer, query, out, cu_seqlens_q, context_lens, block_tables,
-                          max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, stream);
+                          max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale,
+                          workspace, workspace_bytes, stream);
   return launch_generic(layer, query, out, cu_seqlens_q, context_lens, block_tables,
                         max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, stream);
 }

@@ -5,24 +5,29 @@
 // (P cached prefix tokens, possibly shared blocks) with query i seeing KV j iff j <= P + i
 // (cpu.rs:66-68, 87-94). bf16/f16 pools, head_dim 128, block_size 16.
 //
-// CTA = (chunk of 2*TQ query tokens of one sequence, one KV head). GQA is packed into the MMA M
-// dimension: a 128-row Q tile holds TQ = 128 / n_rep tokens x the n_rep query heads that share
-// the KV head, so each K/V tile feeds every head of the group. Two Q tiles (A, B) per CTA share
-// each K/V tile and alternate on the tensor core:
+// Work item = (chunk of 2*TQ query tokens of one sequence, one KV head). GQA is packed into the
+// MMA M dimension: a 128-row Q tile holds TQ = 128 / n_rep tokens x the n_rep query heads that
+// share the KV head, so each K/V tile feeds every head of the group. Two Q tiles (A, B) per item
+// share each K/V tile and alternate on the tensor core:
 //
-//   S_A(i) = Q_A K_i^T ... softmax_A(i) ... PV_A(i) = P_A(i) V_i      (and the same for B)
+//   S_X(i) = Q_X K_i^T ... softmax_X(i) ... PV_X(i) = P_X(i) V_i
 //   issue order: S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) S_A(2) PV_B(1) ...
 //
 // so each softmax warpgroup works while the tensor core runs the other tile's MMAs.
 //
+// Persistent: one CTA per SM; the TMA warp takes work items from a global counter (heaviest
+// chunk of each sequence first) and hands them to the other roles through a 2-slot descriptor
+// ring in shared memory. K/V loads run ahead across item boundaries, and each Q tile is reloaded
+// as soon as the previous item's last MMA reading it has completed.
+//
 // Warp roles (320 threads): warps 0-3 softmax for tile A (thread = TMEM lane = Q row),
-// warps 4-7 softmax for tile B, warp 8 TMA producer, warp 9 MMA issuer + TMEM owner.
+// warps 4-7 softmax for tile B, warp 8 TMA producer + scheduler, warp 9 MMA issuer + TMEM owner.
 //
 // Memory: Q tiles and 2-stage K and V rings in shared memory, all 128-byte swizzled (K-major Q/K,
 // MN-major V). K/V tiles are 128 tokens = 8 pages gathered through the block table with one
 // 16 x 64 TMA box per (page, 64-wide half of head_dim). TMEM (512 columns): S_A, S_B (f32,
-// 128 columns each; P overwrites the first 64 columns as packed 16-bit pairs and feeds the
-// PV MMA straight from TMEM), O_A, O_B (f32 accumulators, 128 columns each).
+// 128 columns each; P overwrites the first 64 columns as packed 16-bit pairs and feeds the PV MMA
+// straight from TMEM), O_A, O_B (f32 accumulators, 128 columns each).
 //
 // Online softmax: running max in log2 units with lazy rescaling: O and the row sum are rescaled
 // only when the max grows by more than 8 (so un-rescaled P stays below 2^8); the final output is
@@ -41,15 +46,16 @@ struct PrefillParams {
   const int32_t *cu_seqlens_q;   // [num_seqs + 1]
   const int32_t *context_lens;   // [num_seqs]
   const int32_t *block_tables;   // [num_seqs, max_blocks_per_seq]
+  int32_t *counters;             // [0] next work item, [1] finished CTAs; both back to 0 at exit
   int32_t max_blocks_per_seq;
-  int32_t num_seqs;
+  int32_t num_seqs;              // <= kPfMaxSeqs per launch
   int32_t num_heads;
   int32_t num_kv_heads;
   int32_t n_rep;
   int32_t num_blocks;
   int32_t total_q;
   int32_t tq;                    // query tokens per Q tile (128 / n_rep)
-  float scale_log2;              // scale * log2(e)
+  float scale_log2;              // scale * log2(e), > 0
 };
 
 constexpr int kPfWarps = 10;
@@ -58,6 +64,13 @@ constexpr int kPfBN = 128;                  // KV tokens per tile
 constexpr int kPfPages = kPfBN / kPage;     // 8 pages per KV tile
 constexpr int kPfStages = 2;
 constexpr float kPfRescale = 8.0f;          // lazy-rescale threshold (log2 units)
+constexpr int kPfMaxSeqs = 2048;            // sequences per launch (chunk table in smem)
+
+struct PfItem {
+  int32_t kind;  // 0 work, 1 invalid sequence data (rows are zeroed), 2 no more work
+  int32_t seq, kvh, t0, q0, S_len, Pfx, n_tiles, n_pages;
+  int32_t pad[7];
+};
 
 struct PrefillSmem {
   static constexpr int kHalf = 128 * 128;                     // 128 rows x 64 values x 2 B
@@ -65,11 +78,15 @@ struct PrefillSmem {
   static constexpr int kQOff = 0;                             // Q_A, Q_B
   static constexpr int kKOff = 2 * kTile;                     // K ring
   static constexpr int kVOff = kKOff + kPfStages * kTile;     // V ring
-  static constexpr int kBarOff = kVOff + kPfStages * kTile;
-  // barrier indices
-  static constexpr int Q = 0, KFULL = 1, KEMPTY = KFULL + kPfStages, VFULL = KEMPTY + kPfStages,
-                       VEMPTY = VFULL + kPfStages, SFULL = VEMPTY + kPfStages, PFULL = SFULL + 2,
-                       ODONE = PFULL + 2, DRAIN = ODONE + 2, NBARS = DRAIN + 1;
+  static constexpr int kOffsOff = kVOff + kPfStages * kTile;  // chunk prefix sums [kPfMaxSeqs+1]
+  static constexpr int kItemOff = kOffsOff + ((kPfMaxSeqs + 1) * 4 + 63) / 64 * 64;
+  static constexpr int kBarOff = kItemOff + 2 * int(sizeof(PfItem));
+  // barrier indices (pairs are indexed by Q tile X or ring stage)
+  static constexpr int QFULL = 0, QEMPTY = 2, KFULL = 4, KEMPTY = KFULL + kPfStages,
+                       VFULL = KEMPTY + kPfStages, VEMPTY = VFULL + kPfStages,
+                       SFULL = VEMPTY + kPfStages, PFULL = SFULL + 2, ODONE = PFULL + 2,
+                       IFULL = ODONE + 2, IEMPTY = IFULL + 2, DRAIN = IEMPTY + 2,
+                       NBARS = DRAIN + 1;
   static constexpr int kMiscOff = kBarOff + NBARS * 8;
   static constexpr int kBytes = kMiscOff + 64;
   static constexpr int kAlloc = kBytes + 1024;
@@ -87,148 +104,152 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
+  int32_t *offs = reinterpret_cast<int32_t *>(smem + S::kOffsOff);
+  PfItem *items = reinterpret_cast<PfItem *>(smem + S::kItemOff);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S::kBarOff);
   uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + S::kMiscOff);
-  int *s_work = reinterpret_cast<int *>(smem + S::kMiscOff + 16);
-  volatile int *s_abort = reinterpret_cast<volatile int *>(smem + S::kMiscOff + 48);
+  volatile int *s_abort = reinterpret_cast<volatile int *>(smem + S::kMiscOff + 16);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kvh = blockIdx.y;
   const int chunk = 2 * p.tq;
-
-  // ---- blockIdx.x -> (sequence, chunk): warp-parallel prefix sum of chunks per sequence ------
-  if (warp == 0) {
-    const int target = blockIdx.x;
-    int base = 0, f_seq = -1, f_local = 0, f_n = 0;
-    for (int s0 = 0; s0 < p.num_seqs && f_seq < 0; s0 += 32) {
-      const int s = s0 + lane;
-      int n = 0;
-      if (s < p.num_seqs) {
-        const int len = p.cu_seqlens_q[s + 1] - p.cu_seqlens_q[s];
-        n = len > 0 ? (len + chunk - 1) / chunk : 0;
-      }
-      int incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      const int excl = incl - n;
-      const unsigned hit =
-          __ballot_sync(0xffffffffu, n > 0 && target >= base + excl && target < base + incl);
-      if (hit) {
-        const int src = __ffs(hit) - 1;
-        f_seq = s0 + src;
-        f_local = __shfl_sync(0xffffffffu, target - base - excl, src);
-        f_n = __shfl_sync(0xffffffffu, n, src);
-      }
-      base += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) {
-      s_work[0] = f_seq;
-      s_work[1] = f_local;
-      s_work[2] = f_n;
-    }
-  }
-  __syncthreads();
-  const int seq = s_work[0];
-  if (seq < 0) return;  // beyond the last chunk (the grid is an upper bound)
-
-  const int q0 = p.cu_seqlens_q[seq];
-  const int S_len = p.cu_seqlens_q[seq + 1] - q0;
-  const int L = p.context_lens[seq];
-  const int Pfx = L - S_len;
-  const int t0 = (s_work[2] - 1 - s_work[1]) * chunk;  // the chunk seeing the most KV runs first
   T *out = static_cast<T *>(p.out);
-  if (L < S_len || int64_t(L) > int64_t(p.max_blocks_per_seq) * kPage || q0 < 0 ||
-      q0 + S_len > p.total_q) {
-    if (tid == 0) report(q0 + S_len > p.total_q || q0 < 0 ? FA_DEVERR_SEQLEN : FA_DEVERR_CONTEXT);
-    const int t_end = min(t0 + chunk, S_len);
-    for (int idx = tid; idx < (t_end - t0) * p.n_rep * 128; idx += kPfThreads) {
-      const int tk = t0 + idx / (p.n_rep * 128), rem = idx % (p.n_rep * 128);
-      const int64_t row = int64_t(q0) + tk;
-      if (row >= 0 && row < p.total_q)
-        out[(row * p.num_heads + kvh * p.n_rep + rem / 128) * 128 + rem % 128] = Elem<T>::from_f(0.f);
-    }
-    return;
-  }
-  const int t_last = min(t0 + chunk, S_len) - 1;
-  const int kv_end = Pfx + t_last + 1;  // KV tokens visible to at least one row of this CTA
-  const int n_tiles = (kv_end + kPfBN - 1) / kPfBN;
-  const int n_pages = (L + kPage - 1) / kPage;
 
+  // ---- chunk table: offs[s] = number of chunks of sequences < s -----------------------------
+  for (int s = tid; s < p.num_seqs; s += kPfThreads) {
+    const int len = p.cu_seqlens_q[s + 1] - p.cu_seqlens_q[s];
+    offs[s + 1] = len > 0 ? (len + chunk - 1) / chunk : 0;
+  }
   if (tid == 0) {
 #pragma unroll 1
-    for (int i = 0; i < S::NBARS; ++i) mbar_init(bar(i), (i == S::PFULL || i == S::PFULL + 1) ? 128 : 1);
+    for (int i = 0; i < S::NBARS; ++i) {
+      const int count = (i == S::PFULL || i == S::PFULL + 1) ? 128
+                        : (i == S::IEMPTY || i == S::IEMPTY + 1) ? 257 : 1;
+      mbar_init(bar(i), count);
+    }
     *s_abort = 0;
+    offs[0] = 0;
     fence_mbar_init();
   }
   if (warp == 9) {
     tc::alloc(smem_u32(s_tmem), 512);
     tc::relinquish();
   }
+  __syncthreads();
+  if (warp == 0) {
+    int carry = 0;
+    for (int s0 = 0; s0 < p.num_seqs; s0 += 32) {
+      const int s = s0 + lane;
+      const int n = s < p.num_seqs ? offs[s + 1] : 0;
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (s < p.num_seqs) offs[s + 1] = carry + incl;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *s_tmem;
+  const int n_items = offs[p.num_seqs] * p.num_kv_heads;
 
   if (warp == 8) {
-    // ================= TMA producer =================
+    // ================= scheduler + TMA producer =================
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar(S::Q), 2 * 2 * 64 * p.n_rep * p.tq * 2);
-#pragma unroll
-      for (int X = 0; X < 2; ++X)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(sbase + S::kQOff + X * S::kTile + hf * S::kHalf, &tm_q, bar(S::Q), hf * 64,
-                      kvh * p.n_rep, q0 + t0 + X * p.tq);
-      const int32_t *table = p.block_tables + size_t(seq) * p.max_blocks_per_seq;
+      int g = 0, v = 0;  // tiles and valid items issued so far
       bool bad = false;
-      int issued = 0;
-      for (int i = 0; i < n_tiles; ++i) {
-        if (*s_abort) break;
-        const int st = i % kPfStages;
-        const uint32_t ph = ((i / kPfStages) - 1) & 1;
-        int rows[kPfPages];
-#pragma unroll
-        for (int j = 0; j < kPfPages; ++j) {
-          int id = table[min(i * kPfPages + j, n_pages - 1)];  // pages past the end: reload the last
-          if (uint32_t(id) >= uint32_t(p.num_blocks)) {
-            bad = true;
-            id = 0;
+      for (int k = 0;; ++k) {
+        const int slot = k & 1;
+        if (k >= 2 && !mbar_wait(bar(S::IEMPTY + slot), ((k >> 1) - 1) & 1)) { *s_abort = 1; break; }
+        PfItem it{};
+        const int w = *s_abort ? n_items : atomicAdd(p.counters, 1);
+        if (w >= n_items) {
+          it.kind = 2;
+        } else {
+          const int c = w / p.num_kv_heads;
+          it.kvh = w % p.num_kv_heads;
+          int lo = 0, hi = p.num_seqs;  // last s with offs[s] <= c
+          while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (offs[mid] <= c) lo = mid; else hi = mid;
           }
-          rows[j] = (id * p.num_kv_heads + kvh) * kPage;
+          it.seq = lo;
+          it.t0 = (offs[lo + 1] - 1 - c) * chunk;  // last chunk (most KV) of a sequence first
+          it.q0 = p.cu_seqlens_q[lo];
+          it.S_len = p.cu_seqlens_q[lo + 1] - it.q0;
+          const int L = p.context_lens[lo];
+          it.Pfx = L - it.S_len;
+          if (L < it.S_len || int64_t(L) > int64_t(p.max_blocks_per_seq) * kPage || it.q0 < 0 ||
+              it.q0 + it.S_len > p.total_q) {
+            it.kind = 1;
+            report(it.q0 < 0 || it.q0 + it.S_len > p.total_q ? FA_DEVERR_SEQLEN : FA_DEVERR_CONTEXT);
+          } else {
+            it.kind = 0;
+            const int kv_end = it.Pfx + min(it.t0 + chunk, it.S_len);
+            it.n_tiles = (kv_end + kPfBN - 1) / kPfBN;
+            it.n_pages = (L + kPage - 1) / kPage;
+          }
         }
-        if (i >= kPfStages && !mbar_wait(bar(S::KEMPTY + st), ph)) { *s_abort = 1; break; }
-        mbar_arrive_expect_tx(bar(S::KFULL + st), S::kTile);
-        const uint32_t kb = sbase + S::kKOff + st * S::kTile;
+        items[slot] = it;
+        mbar_arrive(bar(S::IFULL + slot));
+        if (it.kind == 2) break;
+        if (it.kind == 1) continue;
+        // Q tiles of this item (each waits for the previous item's last S MMA reading it).
+        const int qbytes = 2 * 64 * p.n_rep * p.tq * 2;
+        bool ok = true;
 #pragma unroll
-        for (int j = 0; j < kPfPages; ++j) {
-          tma_load_2d(kb + j * 2048, &tm_k, bar(S::KFULL + st), 0, rows[j]);
-          tma_load_2d(kb + S::kHalf + j * 2048, &tm_k, bar(S::KFULL + st), 64, rows[j]);
-        }
-        if (i >= kPfStages && !mbar_wait(bar(S::VEMPTY + st), ph)) { *s_abort = 1; ++issued; break; }
-        mbar_arrive_expect_tx(bar(S::VFULL + st), S::kTile);
-        const uint32_t vb = sbase + S::kVOff + st * S::kTile;
+        for (int X = 0; X < 2; ++X) {
+          if (v >= 1 && !mbar_wait(bar(S::QEMPTY + X), (v - 1) & 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(bar(S::QFULL + X), qbytes);
 #pragma unroll
-        for (int j = 0; j < kPfPages; ++j) {
-          tma_load_2d(vb + j * 2048, &tm_v, bar(S::VFULL + st), 0, rows[j]);
-          tma_load_2d(vb + S::kHalf + j * 2048, &tm_v, bar(S::VFULL + st), 64, rows[j]);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d(sbase + S::kQOff + X * S::kTile + hf * S::kHalf, &tm_q, bar(S::QFULL + X),
+                        hf * 64, it.kvh * p.n_rep, it.q0 + it.t0 + X * p.tq);
         }
-        ++issued;
+        if (!ok) { *s_abort = 1; break; }
+        const int32_t *table = p.block_tables + size_t(it.seq) * p.max_blocks_per_seq;
+        for (int i = 0; i < it.n_tiles && ok; ++i, ++g) {
+          const int st = g % kPfStages;
+          const uint32_t ph = ((g / kPfStages) - 1) & 1;
+          int rows[kPfPages];
+#pragma unroll
+          for (int j = 0; j < kPfPages; ++j) {
+            int id = table[min(i * kPfPages + j, it.n_pages - 1)];  // past the end: reload the last
+            if (uint32_t(id) >= uint32_t(p.num_blocks)) {
+              bad = true;
+              id = 0;
+            }
+            rows[j] = (id * p.num_kv_heads + it.kvh) * kPage;
+          }
+          if (g >= kPfStages && !mbar_wait(bar(S::KEMPTY + st), ph)) { ok = false; break; }
+          mbar_arrive_expect_tx(bar(S::KFULL + st), S::kTile);
+          const uint32_t kb = sbase + S::kKOff + st * S::kTile;
+#pragma unroll
+          for (int j = 0; j < kPfPages; ++j) {
+            tma_load_2d(kb + j * 2048, &tm_k, bar(S::KFULL + st), 0, rows[j]);
+            tma_load_2d(kb + S::kHalf + j * 2048, &tm_k, bar(S::KFULL + st), 64, rows[j]);
+          }
+          if (g >= kPfStages && !mbar_wait(bar(S::VEMPTY + st), ph)) { ok = false; break; }
+          mbar_arrive_expect_tx(bar(S::VFULL + st), S::kTile);
+          const uint32_t vb = sbase + S::kVOff + st * S::kTile;
+#pragma unroll
+          for (int j = 0; j < kPfPages; ++j) {
+            tma_load_2d(vb + j * 2048, &tm_v, bar(S::VFULL + st), 0, rows[j]);
+            tma_load_2d(vb + S::kHalf + j * 2048, &tm_v, bar(S::VFULL + st), 64, rows[j]);
+          }
+        }
+        if (!ok) { *s_abort = 1; break; }
+        ++v;
       }
       if (bad) report(FA_DEVERR_BLOCK_ID);
-      if (*s_abort) {
-        // Let the loads already issued land before the CTA can exit (bounded waits).
-        for (int i = max(0, issued - kPfStages); i < issued; ++i) {
-          mbar_wait(bar(S::KFULL + i % kPfStages), (i / kPfStages) & 1);
-          mbar_wait(bar(S::VFULL + i % kPfStages), (i / kPfStages) & 1);
-        }
-      }
+      if (*s_abort) report(FA_DEVERR_TIMEOUT);
     }
   } else if (warp == 9) {
     // ================= MMA issuer (one thread) =================
@@ -253,39 +274,60 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                      tc::sw128_desc(vb + k * 2048, S::kHalf, 1024), id_o,
                      (!first || k > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(bar(S::Q), 0) && mbar_wait(bar(S::KFULL), 0);
-      if (ok) {
-        tc::fence_after();
-        issue_s(0, 0);
-        tc::commit(bar(S::SFULL + 0));
-        issue_s(1, 0);
-        tc::commit(bar(S::SFULL + 1));
-        tc::commit(bar(S::KEMPTY + 0));
-      }
-      for (int i = 0; ok && i < n_tiles; ++i) {
-        const int st = i % kPfStages, st1 = (i + 1) % kPfStages;
-        const uint32_t ph = (i / kPfStages) & 1, ph1 = ((i + 1) / kPfStages) & 1;
-        const bool last = i + 1 == n_tiles;
-        if (!(ok = mbar_wait(bar(S::PFULL + 0), i & 1) && mbar_wait(bar(S::VFULL + st), ph))) break;
-        tc::fence_after();
-        issue_pv(0, st, i == 0);
-        if (last) tc::commit(bar(S::ODONE + 0));
-        if (!last) {
-          if (!(ok = mbar_wait(bar(S::KFULL + st1), ph1))) break;
+      int g = 0, v = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!(ok = mbar_wait(bar(S::IFULL + slot), (k >> 1) & 1))) break;
+        const PfItem it = items[slot];
+        if (it.kind == 2) break;
+        if (it.kind == 0) {
+          const int n = it.n_tiles;
+          if (!(ok = mbar_wait(bar(S::QFULL + 0), v & 1) &&
+                     mbar_wait(bar(S::KFULL + g % kPfStages), (g / kPfStages) & 1))) break;
           tc::fence_after();
-          issue_s(0, st1);
+          issue_s(0, g % kPfStages);
           tc::commit(bar(S::SFULL + 0));
-        }
-        if (!(ok = mbar_wait(bar(S::PFULL + 1), i & 1))) break;
-        tc::fence_after();
-        issue_pv(1, st, i == 0);
-        tc::commit(bar(S::VEMPTY + st));
-        if (last) tc::commit(bar(S::ODONE + 1));
-        if (!last) {
-          issue_s(1, st1);
+          if (n == 1) tc::commit(bar(S::QEMPTY + 0));
+          if (!(ok = mbar_wait(bar(S::QFULL + 1), v & 1))) break;
+          tc::fence_after();
+          issue_s(1, g % kPfStages);
           tc::commit(bar(S::SFULL + 1));
-          tc::commit(bar(S::KEMPTY + st1));
+          tc::commit(bar(S::KEMPTY + g % kPfStages));
+          if (n == 1) tc::commit(bar(S::QEMPTY + 1));
+          for (int i = 0; ok && i < n; ++i) {
+            const int gi = g + i;
+            const int st = gi % kPfStages, st1 = (gi + 1) % kPfStages;
+            const uint32_t ph = (gi / kPfStages) & 1, ph1 = ((gi + 1) / kPfStages) & 1;
+            const bool last = i + 1 == n;
+            if (!(ok = mbar_wait(bar(S::PFULL + 0), gi & 1) && mbar_wait(bar(S::VFULL + st), ph))) break;
+            tc::fence_after();
+            issue_pv(0, st, i == 0);
+            if (last) tc::commit(bar(S::ODONE + 0));
+            if (!last) {
+              if (!(ok = mbar_wait(bar(S::KFULL + st1), ph1))) break;
+              tc::fence_after();
+              issue_s(0, st1);
+              tc::commit(bar(S::SFULL + 0));
+              if (i + 2 == n) tc::commit(bar(S::QEMPTY + 0));
+            }
+            if (!(ok = mbar_wait(bar(S::PFULL + 1), gi & 1))) break;
+            tc::fence_after();
+            issue_pv(1, st, i == 0);
+            tc::commit(bar(S::VEMPTY + st));
+            if (last) tc::commit(bar(S::ODONE + 1));
+            if (!last) {
+              issue_s(1, st1);
+              tc::commit(bar(S::SFULL + 1));
+              tc::commit(bar(S::KEMPTY + st1));
+              if (i + 2 == n) tc::commit(bar(S::QEMPTY + 1));
+            }
+          }
+          if (!ok) break;
+          g += n;
+          ++v;
         }
+        mbar_arrive(bar(S::IEMPTY + slot));
       }
       if (!ok) {
         *s_abort = 1;
@@ -301,86 +343,102 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t lane_off = uint32_t(wq * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + X * 128;
     const uint32_t o_addr = tmem + lane_off + 256 + X * 128;
-    const int tok = t0 + X * p.tq + r / p.n_rep;
-    const bool row_valid = r < p.tq * p.n_rep && tok < S_len;
-    const int limit = Pfx + tok;  // visible KV positions j <= limit
     const float sl2 = p.scale_log2;
-    float m_run = neg_inf(), l = 0.f;
+    const bool row_used = r < p.tq * p.n_rep;
+    int g = 0, v = 0;
     bool ok = true;
-    for (int i = 0; i < n_tiles; ++i) {
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::SFULL + X), i & 1)))) break;
-      tc::fence_after();
-      uint32_t sr[4][32];
+    for (int k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::IFULL + slot), (k >> 1) & 1)))) break;
+      const PfItem it = items[slot];
+      if (it.kind == 2) break;
+      const int tok = it.t0 + X * p.tq + r / p.n_rep;
+      const bool row_valid = row_used && tok < it.S_len;
+      T *orow = out + (size_t(it.q0 + min(tok, max(it.S_len - 1, 0))) * p.num_heads +
+                       it.kvh * p.n_rep + r % p.n_rep) * 128;
+      if (it.kind == 1) {
+        const int64_t row = int64_t(it.q0) + tok;
+        if (row_valid && row >= 0 && row < p.total_q) {
+          uint4 *dst = reinterpret_cast<uint4 *>(orow);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld32(s_addr + c * 32, sr[c]);
-      tc::wait_ld();
-      const int j0 = i * kPfBN;
-      float mt = neg_inf();
-      if (j0 + kPfBN - 1 > limit) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = (j0 + c * 32 + e > limit) ? neg_inf() : __uint_as_float(sr[c][e]) * sl2;
-            sr[c][e] = __float_as_uint(x);
-            mt = fmaxf(mt, x);
-          }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = __uint_as_float(sr[c][e]) * sl2;
-            sr[c][e] = __float_as_uint(x);
-            mt = fmaxf(mt, x);
-          }
-      }
-      float factor = 1.f;
-      bool rescale = false;
-      if (i == 0) {
-        m_run = mt;
-      } else if (mt > m_run + kPfRescale) {
-        factor = ex2(m_run - mt);
-        m_run = mt;
-        rescale = true;
-      }
-      const float m_use = m_run == neg_inf() ? 0.f : m_run;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float a = ex2(__uint_as_float(sr[c][2 * e]) - m_use);
-          const float b = ex2(__uint_as_float(sr[c][2 * e + 1]) - m_use);
-          rs += a + b;
-          pk[e] = pack2<T>(a, b);
+          for (int c = 0; c < 16; ++c) dst[c] = make_uint4(0, 0, 0, 0);
         }
-        tc::st16(s_addr + c * 16, pk);  // P: token 2e,2e+1 of chunk c -> column c*16 + e
+        mbar_arrive(bar(S::IEMPTY + slot));
+        continue;
       }
-      l = l * factor + rs;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_X holds PV_X(i-1) (S_X(i) was committed after it): rescale in place.
-#pragma unroll 1
+      const int limit = it.Pfx + tok;  // visible KV positions j <= limit
+      float m_run = neg_inf(), l = 0.f;
+      for (int i = 0; i < it.n_tiles; ++i) {
+        const int gi = g + i;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::SFULL + X), gi & 1)))) break;
+        tc::fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc::ld32(s_addr + c * 32, sr[c]);
+        tc::wait_ld();
+        // Row max on the raw scores (scale > 0); keys past the causal limit become -inf.
+        const int j0 = i * kPfBN;
+        float mx = neg_inf();
+        if (j0 + kPfBN - 1 > limit) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (j0 + c * 32 + e > limit) sr[c][e] = __float_as_uint(neg_inf());
+              mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+            }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+        }
+        const float mt = mx * sl2;
+        float factor = 1.f;
+        bool rescale = false;
+        if (i == 0) {
+          m_run = mt;
+        } else if (mt > m_run + kPfRescale) {
+          factor = ex2(m_run - mt);
+          m_run = mt;
+          rescale = true;
+        }
+        const float neg_m = m_run == neg_inf() ? 0.f : -m_run;
+        float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tc::ld32(o_addr + c * 32, o);
-          tc::wait_ld();
+          uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-          tc::st32(o_addr + c * 32, o);
+          for (int e = 0; e < 16; ++e) {
+            const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, neg_m));
+            const float b = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, neg_m));
+            rs0 += a;
+            rs1 += b;
+            pk[e] = pack2<T>(a, b);
+          }
+          tc::st16(s_addr + c * 16, pk);  // P: tokens 2e, 2e+1 of chunk c -> column c*16 + e
         }
+        l = l * factor + (rs0 + rs1);
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O_X holds PV_X(i-1) (S_X(i) was committed after it): rescale in place.
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tc::ld32(o_addr + c * 32, o);
+            tc::wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tc::st32(o_addr + c * 32, o);
+          }
+        }
+        tc::wait_st();
+        tc::fence_before();
+        mbar_arrive(bar(S::PFULL + X));
       }
-      tc::wait_st();
-      tc::fence_before();
-      mbar_arrive(bar(S::PFULL + X));
-    }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(S::ODONE + X), 0));
-    if (ok) {
+      if (!ok) break;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::ODONE + X), v & 1)))) break;
       tc::fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T *orow = out + (size_t(q0 + min(tok, S_len - 1)) * p.num_heads + kvh * p.n_rep +
-                       r % p.n_rep) * 128;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -393,10 +451,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             pk[e] = pack2<T>(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
           uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-    } else {
+      tc::fence_before();
+      mbar_arrive(bar(S::IEMPTY + slot));
+      g += it.n_tiles;
+      ++v;
+    }
+    if (!ok) {
       *s_abort = 1;
       if (lane == 0) report(FA_DEVERR_TIMEOUT);
     }
@@ -407,6 +470,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == 9) {
     tc::fence_after();
     tc::dealloc(tmem, 512);
+  }
+  if (tid == 0) {
+    // The last CTA to finish returns the work counters to zero for the next launch.
+    __threadfence();
+    if (atomicAdd(&p.counters[1], 1) == int(gridDim.x) - 1) {
+      atomicExch(&p.counters[0], 0);
+      atomicExch(&p.counters[1], 0);
+    }
   }
 }
 

@@ -81,8 +81,8 @@ def test_host_validation_rejects_before_launch():
 
 def test_workspace_sizes():
     L = lib()
-    # Prefill needs no workspace; short decode contexts fit in one split.
-    assert L.fa_paged_attention_workspace_size(16, 32, 8, 128, 2048, 2048) == 0
+    # Prefill needs only its two work counters.
+    assert L.fa_paged_attention_workspace_size(16, 32, 8, 128, 2048, 2048) == 256
     # C2 decode: 64 sequences x 8 kv heads, contexts up to 4096 -> split-K partials.
     ws = L.fa_paged_attention_workspace_size(64, 32, 8, 128, 4096, 1)
     assert ws > 64 * 32 * 128 * 4

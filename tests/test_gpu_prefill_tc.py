@@ -103,6 +103,30 @@ def test_prefill_repeatable(device):
     assert torch.equal(o1, o2)
 
 
+def test_many_sequences_share_one_persistent_launch(device):
+    # 300 short sequences (more work items than SMs, several per CTA) plus a long one.
+    rng = np.random.default_rng(9)
+    lens = list(rng.integers(1, 90, size=300)) + [1700]
+    prefix = [int(x) // 2 // 16 * 16 for x in lens]
+    run_and_check(build(device, LLAMA8B, lens, prefix, 9))
+
+
+def test_invalid_context_zeroes_rows_and_reports(device):
+    b = build(device, LLAMA8B, [300, 200], [0, 0], 10)
+    ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
+    ctx = b.context_lens.clone()
+    ctx[0] = 100  # shorter than its 300 query tokens
+    ops.device_status()
+    out = ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, ctx,
+                            b.block_tables, 4, 1 / math.sqrt(128), b.max_seqlen_q,
+                            b.max_context_len, ops.Workspace(device))
+    assert ops.device_status() & _lib.FA_DEVERR_CONTEXT
+    assert float(out[:300].float().abs().sum()) == 0.0
+    good = oracle_attention(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                            b.block_tables, 4, 1 / math.sqrt(128))
+    assert max_abs(f32(out[300:]), good[300:]) <= TOL
+
+
 def test_bad_block_id_reported(device):
     b = build(device, LLAMA8B, [300, 200], [0, 0], 8)
     ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
@@ -110,5 +134,5 @@ def test_bad_block_id_reported(device):
     bt[1, 2] = 1 << 20
     ops.device_status()
     ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens, bt, 4,
-                      1 / math.sqrt(128), b.max_seqlen_q, b.max_context_len)
+                      1 / math.sqrt(128), b.max_seqlen_q, b.max_context_len, ops.Workspace(device))
     assert ops.device_status() & _lib.FA_DEVERR_BLOCK_ID
