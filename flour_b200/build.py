@@ -41,15 +41,20 @@ def needs_build() -> bool:
     return any(s.stat().st_mtime > t for s in sources())
 
 
-def build(verbose: bool = False, force: bool = False) -> Path:
-    if not force and not needs_build():
+def build(verbose: bool = False, force: bool = False, out: Path | None = None,
+          defines: tuple[str, ...] = ()) -> Path:
+    """Compile the library to `out` (default: the in-tree libflour_attn.so). `defines` are extra
+    -D tuning values (e.g. "FA_PF_POLY_EVERY=2") for building variants outside the tree."""
+    target = Path(out) if out is not None else LIB
+    if out is None and not defines and not force and not needs_build():
         return LIB
     cmd = [
         nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
         "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
         "-I", str(ROOT / "include"), "-I", str(CSRC),
         "-cudart", "static",
-        "-o", str(LIB), str(CSRC / "flour_attn.cu"),
+        *[f"-D{d}" for d in defines],
+        "-o", str(target), str(CSRC / "flour_attn.cu"),
     ]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
@@ -59,7 +64,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         raise RuntimeError("nvcc failed building libflour_attn.so")
     if verbose:
         sys.stderr.write(r.stderr)
-    return LIB
+    return target
 
 
 if __name__ == "__main__":

@@ -66,6 +66,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 256-bit global store (one full 32-byte sector); the address must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void *ptr, const uint32_t *r) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // ---- mbarrier -------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

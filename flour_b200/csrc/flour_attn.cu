@@ -260,7 +260,7 @@ bool prefill_fast_path(const fa_kv_layer *L, int n_rep, int total_q, float scale
   return (L->dtype == FA_BF16 || L->dtype == FA_F16) && L->block_size == fa::kPage &&
          L->head_dim == 128 && n_rep >= 1 && n_rep <= 128 && total_q >= 128 && scale > 0.f &&
          int64_t(L->num_blocks) * L->num_kv_heads * L->block_size < (int64_t(1) << 31) &&
-         aligned(L->k_cache, 16) && aligned(L->v_cache, 16) && aligned(q, 16) && aligned(out, 16);
+         aligned(L->k_cache, 16) && aligned(L->v_cache, 16) && aligned(q, 16) && aligned(out, 32);
 }
 
 // Bytes of workspace the prefill kernel needs: two work counters (zero-filled once by the caller,

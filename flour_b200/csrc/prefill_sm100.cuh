@@ -165,42 +165,56 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma_prefetch_desc(&tm_v);
       int g = 0, v = 0;  // tiles and valid items issued so far
       bool bad = false;
-      for (int k = 0;; ++k) {
-        const int slot = k & 1;
-        if (k >= 2 && !mbar_wait(bar(S::IEMPTY + slot), ((k >> 1) - 1) & 1)) { *s_abort = 1; break; }
-        PfItem it{};
+      // Next work item: global ticket + the sequence's metadata. Called one item ahead, where the
+      // producer would otherwise wait for a free ring stage, so its latency stays hidden.
+      auto fetch = [&](PfItem &it) {
+        it = PfItem{};
         const int w = *s_abort ? n_items : atomicAdd(p.counters, 1);
         if (w >= n_items) {
           it.kind = 2;
-        } else {
-          const int c = w / p.num_kv_heads;
-          it.kvh = w % p.num_kv_heads;
-          int lo = 0, hi = p.num_seqs;  // last s with offs[s] <= c
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (offs[mid] <= c) lo = mid; else hi = mid;
-          }
-          it.seq = lo;
-          it.t0 = (offs[lo + 1] - 1 - c) * chunk;  // last chunk (most KV) of a sequence first
-          it.q0 = p.cu_seqlens_q[lo];
-          it.S_len = p.cu_seqlens_q[lo + 1] - it.q0;
-          const int L = p.context_lens[lo];
-          it.Pfx = L - it.S_len;
-          if (L < it.S_len || int64_t(L) > int64_t(p.max_blocks_per_seq) * kPage || it.q0 < 0 ||
-              it.q0 + it.S_len > p.total_q) {
-            it.kind = 1;
-            report(it.q0 < 0 || it.q0 + it.S_len > p.total_q ? FA_DEVERR_SEQLEN : FA_DEVERR_CONTEXT);
-          } else {
-            it.kind = 0;
-            const int kv_end = it.Pfx + min(it.t0 + chunk, it.S_len);
-            it.n_tiles = (kv_end + kPfBN - 1) / kPfBN;
-            it.n_pages = (L + kPage - 1) / kPage;
-          }
+          return;
         }
+        const int c = w / p.num_kv_heads;
+        it.kvh = w % p.num_kv_heads;
+        int lo = 0, hi = p.num_seqs;  // last s with offs[s] <= c
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (offs[mid] <= c) lo = mid; else hi = mid;
+        }
+        it.seq = lo;
+        it.t0 = (offs[lo + 1] - 1 - c) * chunk;  // last chunk (most KV) of a sequence first
+        it.q0 = p.cu_seqlens_q[lo];
+        it.S_len = p.cu_seqlens_q[lo + 1] - it.q0;
+        const int L = p.context_lens[lo];
+        it.Pfx = L - it.S_len;
+        if (L < it.S_len || int64_t(L) > int64_t(p.max_blocks_per_seq) * kPage || it.q0 < 0 ||
+            it.q0 + it.S_len > p.total_q) {
+          it.kind = 1;
+          report(it.q0 < 0 || it.q0 + it.S_len > p.total_q ? FA_DEVERR_SEQLEN : FA_DEVERR_CONTEXT);
+        } else {
+          it.kind = 0;
+          const int kv_end = it.Pfx + min(it.t0 + chunk, it.S_len);
+          it.n_tiles = (kv_end + kPfBN - 1) / kPfBN;
+          it.n_pages = (L + kPage - 1) / kPage;
+        }
+      };
+      PfItem next;
+      fetch(next);
+      for (int k = 0;; ++k) {
+        const int slot = k & 1;
+        const PfItem it = next;
+        if (k >= 2 && !mbar_wait(bar(S::IEMPTY + slot), ((k >> 1) - 1) & 1)) { *s_abort = 1; break; }
         items[slot] = it;
         mbar_arrive(bar(S::IFULL + slot));
         if (it.kind == 2) break;
-        if (it.kind == 1) continue;
+        if (it.kind == 1) {
+          fetch(next);
+          continue;
+        }
+        const int32_t *table = p.block_tables + size_t(it.seq) * p.max_blocks_per_seq;
+        int ids[kPfPages];  // block ids of the tile being issued (loaded one tile ahead)
+#pragma unroll
+        for (int j = 0; j < kPfPages; ++j) ids[j] = table[min(j, it.n_pages - 1)];
         // Q tiles of this item (each waits for the previous item's last S MMA reading it).
         const int qbytes = 2 * 64 * p.n_rep * p.tq * 2;
         bool ok = true;
@@ -214,19 +228,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         hf * 64, it.kvh * p.n_rep, it.q0 + it.t0 + X * p.tq);
         }
         if (!ok) { *s_abort = 1; break; }
-        const int32_t *table = p.block_tables + size_t(it.seq) * p.max_blocks_per_seq;
+        // Take the next ticket two tiles before this item's loads end: early enough to hide the
+        // ticket and metadata latency, late enough not to hold work another CTA could start.
+        const int fetch_at = it.n_tiles >= 3 ? it.n_tiles - 2 : it.n_tiles;
         for (int i = 0; i < it.n_tiles && ok; ++i, ++g) {
+          if (i == fetch_at) fetch(next);
           const int st = g % kPfStages;
           const uint32_t ph = ((g / kPfStages) - 1) & 1;
-          int rows[kPfPages];
+          int rows[kPfPages], nids[kPfPages];
 #pragma unroll
           for (int j = 0; j < kPfPages; ++j) {
-            int id = table[min(i * kPfPages + j, it.n_pages - 1)];  // past the end: reload the last
+            int id = ids[j];
             if (uint32_t(id) >= uint32_t(p.num_blocks)) {
               bad = true;
               id = 0;
             }
             rows[j] = (id * p.num_kv_heads + it.kvh) * kPage;
+            // next tile's ids: in flight while this tile waits for its ring stage
+            nids[j] = table[min((i + 1) * kPfPages + j, it.n_pages - 1)];
           }
           if (g >= kPfStages && !mbar_wait(bar(S::KEMPTY + st), ph)) { ok = false; break; }
           mbar_arrive_expect_tx(bar(S::KFULL + st), S::kTile);
@@ -244,8 +263,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tma_load_2d(vb + j * 2048, &tm_v, bar(S::VFULL + st), 0, rows[j]);
             tma_load_2d(vb + S::kHalf + j * 2048, &tm_v, bar(S::VFULL + st), 64, rows[j]);
           }
+#pragma unroll
+          for (int j = 0; j < kPfPages; ++j) ids[j] = nids[j];
         }
         if (!ok) { *s_abort = 1; break; }
+        if (fetch_at == it.n_tiles) fetch(next);
         ++v;
       }
       if (bad) report(FA_DEVERR_BLOCK_ID);
@@ -359,9 +381,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (it.kind == 1) {
         const int64_t row = int64_t(it.q0) + tok;
         if (row_valid && row >= 0 && row < p.total_q) {
-          uint4 *dst = reinterpret_cast<uint4 *>(orow);
+          const uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-          for (int c = 0; c < 16; ++c) dst[c] = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < 8; ++c) st_global_v8(orow + c * 16, z);
         }
         mbar_arrive(bar(S::IEMPTY + slot));
         continue;
@@ -377,22 +399,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int c = 0; c < 4; ++c) tc::ld32(s_addr + c * 32, sr[c]);
         tc::wait_ld();
         // Row max on the raw scores (scale > 0); keys past the causal limit become -inf.
+        // Eight independent partial maxima / sums keep the dependency chains short.
         const int j0 = i * kPfBN;
-        float mx = neg_inf();
+        float mxp[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mxp[q] = neg_inf();
         if (j0 + kPfBN - 1 > limit) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               if (j0 + c * 32 + e > limit) sr[c][e] = __float_as_uint(neg_inf());
-              mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+              mxp[e & 7] = fmaxf(mxp[e & 7], __uint_as_float(sr[c][e]));
             }
         } else {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+            for (int e = 0; e < 32; ++e) mxp[e & 7] = fmaxf(mxp[e & 7], __uint_as_float(sr[c][e]));
         }
+        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
         const float mt = mx * sl2;
         float factor = 1.f;
         bool rescale = false;
@@ -404,7 +431,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           rescale = true;
         }
         const float neg_m = m_run == neg_inf() ? 0.f : -m_run;
-        float rs0 = 0.f, rs1 = 0.f;
+        float rsp[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rsp[q] = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
@@ -412,12 +441,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           for (int e = 0; e < 16; ++e) {
             const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, neg_m));
             const float b = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, neg_m));
-            rs0 += a;
-            rs1 += b;
+            rsp[(2 * e) & 7] += a;
+            rsp[(2 * e + 1) & 7] += b;
             pk[e] = pack2<T>(a, b);
           }
           tc::st16(s_addr + c * 16, pk);  // P: tokens 2e, 2e+1 of chunk c -> column c*16 + e
         }
+        const float rs0 = (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
+        const float rs1 = (rsp[4] + rsp[5]) + (rsp[6] + rsp[7]);
         l = l * factor + (rs0 + rs1);
         if (__any_sync(0xffffffffu, rescale)) {
           // O_X holds PV_X(i-1) (S_X(i) was committed after it): rescale in place.
@@ -449,9 +480,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             pk[e] = pack2<T>(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-          uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          // Two full 32-byte sectors per store: each row is written by one thread, so wider
+          // stores mean fewer scattered transactions clogging the load/store pipe.
+          st_global_v8(orow + c * 32, pk);
+          st_global_v8(orow + c * 32 + 16, pk + 8);
         }
       }
       tc::fence_before();

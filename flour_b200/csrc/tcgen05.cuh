@@ -112,6 +112,13 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// Copy a 128-row x 256-bit (16 values of 16 bits per row) matrix, described by a shared-memory
+// matrix descriptor, into TMEM: row r -> lane r, its 256 bits -> 8 consecutive columns (the
+// layout an A operand in TMEM uses). Asynchronous and ordered with this thread's tcgen05.mma.
+__device__ __forceinline__ void cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 operation this thread issued so far has completed.
 __device__ __forceinline__ void commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
