@@ -58,13 +58,24 @@ struct PrefillParams {
   float scale_log2;              // scale * log2(e), > 0
 };
 
-constexpr int kPfWarps = 10;
+constexpr int kPfSoftmaxWarps = 16;         // 2 Q tiles x 2 column halves x 4 row quadrants
+constexpr int kPfProducerWarp = kPfSoftmaxWarps;
+constexpr int kPfMmaWarp = kPfSoftmaxWarps + 1;
+constexpr int kPfWarps = kPfSoftmaxWarps + 2;
 constexpr int kPfThreads = kPfWarps * 32;
 constexpr int kPfBN = 128;                  // KV tokens per tile
 constexpr int kPfPages = kPfBN / kPage;     // 8 pages per KV tile
 constexpr int kPfStages = 2;
 constexpr float kPfRescale = 8.0f;          // lazy-rescale threshold (log2 units)
 constexpr int kPfMaxSeqs = 2048;            // sequences per launch (chunk table in smem)
+#ifndef FA_PF_EXP_PACKED
+#define FA_PF_EXP_PACKED 0                  // 1: exponentials as packed 16-bit pairs
+#endif
+constexpr bool kPfExpPacked = FA_PF_EXP_PACKED != 0;
+#ifndef FA_PF_TRUNC_P
+#define FA_PF_TRUNC_P 1                     // bf16 P by truncation (ALU) instead of cvt (SFU)
+#endif
+constexpr bool kPfTruncP = FA_PF_TRUNC_P != 0;
 
 struct PfItem {
   int32_t kind;  // 0 work, 1 invalid sequence data (rows are zeroed), 2 no more work
@@ -80,7 +91,8 @@ struct PrefillSmem {
   static constexpr int kVOff = kKOff + kPfStages * kTile;     // V ring
   static constexpr int kOffsOff = kVOff + kPfStages * kTile;  // chunk prefix sums [kPfMaxSeqs+1]
   static constexpr int kItemOff = kOffsOff + ((kPfMaxSeqs + 1) * 4 + 63) / 64 * 64;
-  static constexpr int kBarOff = kItemOff + 2 * int(sizeof(PfItem));
+  static constexpr int kXchOff = kItemOff + 2 * int(sizeof(PfItem));  // f32 [2 X][2 halves][128]
+  static constexpr int kBarOff = kXchOff + 2 * 2 * 128 * 4;
   // barrier indices (pairs are indexed by Q tile X or ring stage)
   static constexpr int QFULL = 0, QEMPTY = 2, KFULL = 4, KEMPTY = KFULL + kPfStages,
                        VFULL = KEMPTY + kPfStages, VEMPTY = VFULL + kPfStages,
@@ -91,6 +103,22 @@ struct PrefillSmem {
   static constexpr int kBytes = kMiscOff + 64;
   static constexpr int kAlloc = kBytes + 1024;
 };
+
+// Named-barrier helpers for a pair of warps (64 threads). pair_all is a barrier that also ANDs
+// a predicate across both warps, so a bounded wait that times out in one warp ends both.
+__device__ __forceinline__ void pair_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ bool pair_all(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %2, 0;\n\t"
+      "bar.red.and.pred po, %1, 64, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(uint32_t(v))
+      : "memory");
+  return r != 0;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kPfThreads, 1)
@@ -123,15 +151,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (tid == 0) {
 #pragma unroll 1
     for (int i = 0; i < S::NBARS; ++i) {
-      const int count = (i == S::PFULL || i == S::PFULL + 1) ? 128
-                        : (i == S::IEMPTY || i == S::IEMPTY + 1) ? 257 : 1;
+      const int count = (i == S::PFULL || i == S::PFULL + 1) ? 256
+                        : (i == S::IEMPTY || i == S::IEMPTY + 1) ? 1 + 32 * kPfSoftmaxWarps : 1;
       mbar_init(bar(i), count);
     }
     *s_abort = 0;
     offs[0] = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == kPfMmaWarp) {
     tc::alloc(smem_u32(s_tmem), 512);
     tc::relinquish();
   }
@@ -157,7 +185,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *s_tmem;
   const int n_items = offs[p.num_seqs] * p.num_kv_heads;
 
-  if (warp == 8) {
+  if (warp == kPfProducerWarp) {
     // ================= scheduler + TMA producer =================
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -273,7 +301,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (bad) report(FA_DEVERR_BLOCK_ID);
       if (*s_abort) report(FA_DEVERR_TIMEOUT);
     }
-  } else if (warp == 9) {
+  } else if (warp == kPfMmaWarp) {
     // ================= MMA issuer (one thread) =================
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_f16(kBf16, 128, 128, false, false);
@@ -359,31 +387,40 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_wait(bar(S::DRAIN), 0);
     }
   } else {
-    // ================= softmax warpgroups =================
-    const int X = warp >> 2, wq = warp & 3;
+    // ================= softmax warps =================
+    // Warp (X, half, quadrant): rows 32*quadrant.. of Q tile X, S columns [64*half, 64*half+64).
+    // The two warps sharing a row quadrant exchange row maxima / sums through shared memory and
+    // take every wait decision together (reduction barrier), so neither can leave the other
+    // stranded at a barrier.
+    const int X = warp >> 3, hh = (warp >> 2) & 1, wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t lane_off = uint32_t(wq * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + X * 128;
-    const uint32_t o_addr = tmem + lane_off + 256 + X * 128;
+    const uint32_t s_addr = tmem + lane_off + X * 128 + hh * 64;       // this half of S_X
+    const uint32_t p_addr = tmem + lane_off + X * 128 + hh * 32;       // its P columns
+    const uint32_t o_addr = tmem + lane_off + 256 + X * 128 + hh * 64; // this half of O_X
+    const int pair_bar = 1 + X * 4 + wq;  // named barrier of the two warps sharing the rows
+    float *xch = reinterpret_cast<float *>(smem + S::kXchOff);
+    float *xch_own = xch + (X * 2 + hh) * 128 + r;
+    const float *xch_mate = xch + (X * 2 + (hh ^ 1)) * 128 + r;
     const float sl2 = p.scale_log2;
     const bool row_used = r < p.tq * p.n_rep;
     int g = 0, v = 0;
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int slot = k & 1;
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::IFULL + slot), (k >> 1) & 1)))) break;
+      if (!(ok = pair_all(pair_bar, mbar_wait(bar(S::IFULL + slot), (k >> 1) & 1)))) break;
       const PfItem it = items[slot];
       if (it.kind == 2) break;
       const int tok = it.t0 + X * p.tq + r / p.n_rep;
       const bool row_valid = row_used && tok < it.S_len;
       T *orow = out + (size_t(it.q0 + min(tok, max(it.S_len - 1, 0))) * p.num_heads +
-                       it.kvh * p.n_rep + r % p.n_rep) * 128;
+                       it.kvh * p.n_rep + r % p.n_rep) * 128 + hh * 64;
       if (it.kind == 1) {
         const int64_t row = int64_t(it.q0) + tok;
         if (row_valid && row >= 0 && row < p.total_q) {
           const uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-          for (int c = 0; c < 8; ++c) st_global_v8(orow + c * 16, z);
+          for (int c = 0; c < 4; ++c) st_global_v8(orow + c * 16, z);
         }
         mbar_arrive(bar(S::IEMPTY + slot));
         continue;
@@ -392,21 +429,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       float m_run = neg_inf(), l = 0.f;
       for (int i = 0; i < it.n_tiles; ++i) {
         const int gi = g + i;
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::SFULL + X), gi & 1)))) break;
+        if (!(ok = pair_all(pair_bar, mbar_wait(bar(S::SFULL + X), gi & 1)))) break;
         tc::fence_after();
-        uint32_t sr[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tc::ld32(s_addr + c * 32, sr[c]);
+        uint32_t sr[2][32];
+        tc::ld32(s_addr, sr[0]);
+        tc::ld32(s_addr + 32, sr[1]);
         tc::wait_ld();
         // Row max on the raw scores (scale > 0); keys past the causal limit become -inf.
-        // Eight independent partial maxima / sums keep the dependency chains short.
-        const int j0 = i * kPfBN;
+        const int j0 = i * kPfBN + hh * 64;
         float mxp[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) mxp[q] = neg_inf();
-        if (j0 + kPfBN - 1 > limit) {
+        if (j0 + 63 > limit) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               if (j0 + c * 32 + e > limit) sr[c][e] = __float_as_uint(neg_inf());
@@ -414,13 +450,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
         } else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) mxp[e & 7] = fmaxf(mxp[e & 7], __uint_as_float(sr[c][e]));
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-        const float mt = mx * sl2;
+        const float mx_half = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                    fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        *xch_own = mx_half;
+        pair_sync(pair_bar);
+        const float mt = fmaxf(mx_half, *xch_mate) * sl2;  // both halves: the same row max
         float factor = 1.f;
         bool rescale = false;
         if (i == 0) {
@@ -435,7 +473,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) rsp[q] = 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -445,15 +483,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             rsp[(2 * e + 1) & 7] += b;
             pk[e] = pack2<T>(a, b);
           }
-          tc::st16(s_addr + c * 16, pk);  // P: tokens 2e, 2e+1 of chunk c -> column c*16 + e
+          tc::st16(p_addr + c * 16, pk);  // P: tokens 2e, 2e+1 of chunk c -> column c*16 + e
         }
-        const float rs0 = (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
-        const float rs1 = (rsp[4] + rsp[5]) + (rsp[6] + rsp[7]);
-        l = l * factor + (rs0 + rs1);
+        l = l * factor + (((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) +
+                          ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7])));
         if (__any_sync(0xffffffffu, rescale)) {
-          // O_X holds PV_X(i-1) (S_X(i) was committed after it): rescale in place.
+          // O_X holds PV_X(i-1) (S_X(i) was committed after it): rescale this half in place.
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t o[32];
             tc::ld32(o_addr + c * 32, o);
             tc::wait_ld();
@@ -467,11 +504,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         mbar_arrive(bar(S::PFULL + X));
       }
       if (!ok) break;
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(S::ODONE + X), v & 1)))) break;
+      if (!(ok = pair_all(pair_bar, mbar_wait(bar(S::ODONE + X), v & 1)))) break;
       tc::fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      *xch_own = l;
+      pair_sync(pair_bar);
+      const float lt = l + *xch_mate;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tc::ld32(o_addr + c * 32, o);
         tc::wait_ld();
@@ -480,8 +520,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             pk[e] = pack2<T>(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-          // Two full 32-byte sectors per store: each row is written by one thread, so wider
-          // stores mean fewer scattered transactions clogging the load/store pipe.
+          // Two full 32-byte sectors per store: each row half is written by one thread, so
+          // wider stores mean fewer scattered transactions clogging the load/store pipe.
           st_global_v8(orow + c * 32, pk);
           st_global_v8(orow + c * 32 + 16, pk + 8);
         }
@@ -499,7 +539,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kPfMmaWarp) {
     tc::fence_after();
     tc::dealloc(tmem, 512);
   }
