@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-longctx", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -329,6 +330,12 @@ def run_ours(args):
         prefill = run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_ranks,
                               barrier, world)
 
+    # ---- long-context split-K decode (C4) ----------------------------------------------------
+    longctx = None
+    if not args.no_longctx:
+        longctx = run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks,
+                              barrier, world)
+
     # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------------
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
@@ -368,6 +375,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if prefill:
             line["prefill"] = prefill
+        if longctx:
+            line["longctx"] = longctx
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
@@ -498,6 +507,60 @@ def run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_
             "frac_of_measured_peak": round(flops / (kernel_ms / 1e3) / 1e12 / tc_peak, 4),
             "ms_per_layer": round(ms, 4), "suffix_tokens": int(b.q.shape[0]),
             "flops_per_layer": flops}
+
+
+def run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks, barrier, world):
+    """C4: 16 sequences with ctx ~ U[16K, 32K] on one layer's pool sized toward 150 GB (capped by
+    the free device memory less 8 GB), block ids drawn at random from the whole pool; split-K
+    decode, one layer repeated 32 times."""
+    from flour_b200.workloads import LLAMA8B, c4_contexts, make_decode
+    h = LLAMA8B
+    block_bytes = 2 * h.num_kv_heads * h.block_size * h.head_dim * 2  # K and V, bf16
+    free, _ = torch.cuda.mem_get_info(dev)
+    nb = int(min(150e9, max(free - 8e9, 4e9)) // block_bytes)
+    ctx = c4_contexts(seed + 4)
+    b = make_decode(h, ctx, torch.bfloat16, dev, seed + 4, pool_blocks=nb, fill=False)
+    # Only the blocks the tables reference need values; fill them (about 1.6 GB).
+    bt = b.block_tables.cpu().numpy()
+    pages = (b.ctx_host.astype(np.int64) + 15) // 16
+    used = torch.from_numpy(np.concatenate([bt[i, :n] for i, n in enumerate(pages)]).astype(np.int64))
+    gen = torch.Generator(device=dev).manual_seed(seed + 5)
+    for cache in (b.k_caches[0], b.v_caches[0]):
+        for chunk in used.split(4096):
+            idx = chunk.to(dev)
+            cache[idx] = torch.randn((len(chunk),) + tuple(cache.shape[1:]), device=dev,
+                                     generator=gen).to(cache.dtype)
+    scale = 1.0 / math.sqrt(h.head_dim)
+    ws = ops.Workspace(dev)
+    out = torch.empty_like(b.q)
+    reps = 32
+
+    def launch():
+        ops.paged_decode(b.q, b.k_caches[0], b.v_caches[0], b.block_tables, b.context_lens, h.n_rep,
+                         scale, b.max_context_len, ws, out=out)
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+    nbytes = b.kv_bytes_per_layer() + b.io_bytes_per_layer()
+    gbps = nbytes / (ms / 1e3) / 1e9
+    res = {"config": "C4 long-context split-K decode: 16 seqs, ctx ~ U[16384, 32768], Llama-3-8B "
+                     "heads, bf16, block ids random over the whole pool, one layer x32",
+           "gbps": round(gbps * world, 1), "frac_of_measured_peak": round(gbps / hbm_peak, 4),
+           "ms_per_layer": round(ms, 4), "bytes_per_layer": nbytes,
+           "pool_gb": round(nb * block_bytes / 1e9, 1), "mean_ctx": float(np.mean(ctx))}
+    del b, out, ws
+    torch.cuda.empty_cache()
+    return res
 
 
 def main():
