@@ -20,6 +20,7 @@ FA_DEVERR_SLOT = 0x4
 FA_DEVERR_TIMEOUT = 0x8
 FA_DEVERR_SEQLEN = 0x10
 FA_DEVERR_PAIR = 0x20
+FA_DEVERR_POSITION = 0x40
 FA_MAX_COPY_LAYERS = 128
 FA_NOALLOC_DECODE_SCRATCH_BYTES = 8 * 1024 * 1024
 
@@ -43,6 +44,26 @@ class FaKvLayer(ctypes.Structure):
 
 _LP = ctypes.POINTER(FaKvLayer)
 
+
+class FaQkvWeights(ctypes.Structure):
+    """``fa_qkv_weights``: one layer's stacked q/k/v projection weights and RoPE tables."""
+
+    _fields_ = [
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("q_norm_weight", ctypes.c_void_p),
+        ("k_norm_weight", ctypes.c_void_p),
+        ("rms_eps", ctypes.c_float),
+        ("hidden", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("max_position", ctypes.c_int32),
+    ]
+
+
+_WP = ctypes.POINTER(FaQkvWeights)
+
 SIGNATURES = {
     "fa_abi_version": (_I32, []),
     "fa_status_string": (ctypes.c_char_p, [_I32]),
@@ -59,6 +80,8 @@ SIGNATURES = {
     "fa_paged_decode_noalloc": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P]),
     "fa_paged_prefill": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                                 _F, _P, _SZ, _P]),
+    "fa_qkv_rope_cache": (_I32, [_LP, _WP, _P, _P, _P, _I32, _P, _P]),
+    "fa_o_proj_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P]),
 }
 
 

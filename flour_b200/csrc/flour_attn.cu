@@ -11,6 +11,7 @@
 #include "attn_generic.cuh"
 #include "cache_ops.cuh"
 #include "decode_sm100.cuh"
+#include "gemm_sm100.cuh"
 #include "prefill_sm100.cuh"
 #include "flour_attn.h"
 
@@ -377,6 +378,82 @@ fa_status noalloc_scratch(void **out) {
   return FA_OK;
 }
 
+// ---- projection GEMMs ---------------------------------------------------------------------
+
+// 2-D map over a row-major [rows, K] 16-bit matrix: box = box_rows x 64 elements (128 B),
+// 128-byte swizzle (the K-major operand layout of the tcgen05 GEMM).
+fa_status make_gemm_map(CUtensorMap *map, const void *base, int64_t rows, int64_t K, int32_t dt,
+                        int box_rows, const char *who) {
+  if (fa_status s = get_encoder(); s != FA_OK) return s;
+  const CUtensorMapDataType t =
+      dt == FA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  cuuint32_t box[2] = {uint32_t(fa::kGemmBK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, t, 2, const_cast<void *>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", who, int(r));
+  return FA_OK;
+}
+
+// 256-column output tiles when they alone fill the GPU, else 128 (more CTAs for small M).
+int gemm_bn(int M, int N) {
+  const int64_t tiles256 = int64_t((M + 127) / 128) * ((N + 255) / 256);
+  return tiles256 >= sm_count() ? 256 : 128;
+}
+
+template <typename T, int BN, class Epi>
+fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, const void *b,
+                        int32_t dt, cudaStream_t stream, const char *who) {
+  using C = fa::GemmCfg<BN>;
+  fa::GemmShape s{M, N, K, (M + 127) / 128, (N + BN - 1) / BN};
+  CUtensorMap ta, tb;
+  if (fa_status st = make_gemm_map(&ta, a, M, K, dt, 128, who); st != FA_OK) return st;
+  if (fa_status st = make_gemm_map(&tb, b, N, K, dt, BN, who); st != FA_OK) return st;
+  auto kern = fa::gemm_tn_kernel<T, BN, Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: set smem attribute: %s", who, cudaGetErrorString(e));
+  const int grid = int(std::min<int64_t>(sm_count(), int64_t(s.tiles_m) * s.tiles_n));
+  kern<<<grid, fa::kGemmThreads, C::kAlloc, stream>>>(s, epi, ta, tb);
+  return check_launch(who);
+}
+
+template <typename T, class Epi>
+fa_status launch_gemm(int M, int N, int K, const Epi &epi, const void *a, const void *b,
+                      int32_t dt, cudaStream_t stream, const char *who) {
+  if (gemm_bn(M, N) == 256) return launch_gemm_t<T, 256>(M, N, K, epi, a, b, dt, stream, who);
+  return launch_gemm_t<T, 128>(M, N, K, epi, a, b, dt, stream, who);
+}
+
+template <typename T>
+fa_status launch_qkv(const fa_kv_layer *L, const fa_qkv_weights *w, const void *x,
+                     const int32_t *pos, const int32_t *slots, int T_, void *q_out,
+                     cudaStream_t stream) {
+  fa::QkvEpilogue<T> epi{};
+  epi.q_out = static_cast<T *>(q_out);
+  epi.k_cache = static_cast<T *>(L->k_cache);
+  epi.v_cache = static_cast<T *>(L->v_cache);
+  epi.bias = static_cast<const T *>(w->bias);
+  epi.q_norm = static_cast<const T *>(w->q_norm_weight);
+  epi.k_norm = static_cast<const T *>(w->k_norm_weight);
+  epi.rope_cos = w->rope_cos;
+  epi.rope_sin = w->rope_sin;
+  epi.positions = pos;
+  epi.slots = slots;
+  epi.rms_eps = w->rms_eps;
+  epi.num_heads = w->num_heads;
+  epi.num_kv_heads = L->num_kv_heads;
+  epi.head_dim = L->head_dim;
+  epi.num_blocks = L->num_blocks;
+  epi.block_size = L->block_size;
+  epi.max_position = w->max_position;
+  const int N = (w->num_heads + 2 * L->num_kv_heads) * L->head_dim;
+  return launch_gemm<T>(T_, N, w->hidden, epi, x, w->weight, L->dtype, stream, "qkv_rope_cache");
+}
+
 }  // namespace
 
 extern "C" {
@@ -655,4 +732,66 @@ fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, v
                        FA_NOALLOC_DECODE_SCRATCH_BYTES, stream);
 }
 
+fa_status fa_qkv_rope_cache(const fa_kv_layer *layer, const fa_qkv_weights *w, const void *x,
+                            const int32_t *positions, const int32_t *slot_mapping,
+                            int32_t num_tokens, void *q_out, fa_stream_t stream) {
+  const char *who = "qkv_rope_cache";
+  if (fa_status s = check_layer(layer, who); s != FA_OK) return s;
+  if (!w) return fail(FA_EINVAL, "%s: weights is NULL", who);
+  if (num_tokens < 0) return fail(FA_EINVAL, "%s: num_tokens %d < 0", who, num_tokens);
+  if (num_tokens == 0) return ok();
+  if (!x || !positions || !slot_mapping || !q_out || !w->weight || !w->rope_cos || !w->rope_sin)
+    return fail(FA_EINVAL, "%s: NULL x/positions/slot_mapping/q_out/weight/rope tables", who);
+  if (layer->dtype != FA_BF16 && layer->dtype != FA_F16)
+    return fail(FA_EUNSUPPORTED, "%s: pool dtype must be bf16 or f16", who);
+  if (layer->head_dim != 64 && layer->head_dim != 128)
+    return fail(FA_EUNSUPPORTED, "%s: head_dim %d (64 or 128 supported)", who, layer->head_dim);
+  if (w->num_heads <= 0 || w->num_heads % layer->num_kv_heads != 0)
+    return fail(FA_EINVAL, "%s: num_heads %d is not a multiple of num_kv_heads %d", who,
+                w->num_heads, layer->num_kv_heads);
+  if (w->hidden <= 0 || w->hidden % 8 != 0)
+    return fail(FA_EINVAL, "%s: hidden %d must be a positive multiple of 8", who, w->hidden);
+  if (w->max_position <= 0) return fail(FA_EINVAL, "%s: max_position %d", who, w->max_position);
+  if (!(w->rms_eps >= 0.f) || !std::isfinite(w->rms_eps))
+    return fail(FA_EINVAL, "%s: rms_eps must be finite and >= 0", who);
+  if (!aligned(x, 16) || !aligned(w->weight, 16) || !aligned(q_out, 32) ||
+      !aligned(w->rope_cos, 16) || !aligned(w->rope_sin, 16) || !aligned(layer->k_cache, 32) ||
+      !aligned(layer->v_cache, 32))
+    return fail(FA_EINVAL, "%s: misaligned x/weight (16 B), q_out/pools (32 B) or tables (16 B)", who);
+  if (int64_t(num_tokens) * w->num_heads * layer->head_dim >= (int64_t(1) << 40))
+    return fail(FA_ERANGE, "%s: too many tokens", who);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return layer->dtype == FA_BF16
+             ? launch_qkv<__nv_bfloat16>(layer, w, x, positions, slot_mapping, num_tokens, q_out, st)
+             : launch_qkv<__half>(layer, w, x, positions, slot_mapping, num_tokens, q_out, st);
+}
+
+fa_status fa_o_proj_residual(const void *attn, const void *weight, const void *residual, void *out,
+                             int32_t num_tokens, int32_t in_features, int32_t out_features,
+                             int32_t dtype, fa_stream_t stream) {
+  const char *who = "o_proj_residual";
+  if (num_tokens < 0) return fail(FA_EINVAL, "%s: num_tokens %d < 0", who, num_tokens);
+  if (num_tokens == 0) return ok();
+  if (!attn || !weight || !out) return fail(FA_EINVAL, "%s: NULL attn/weight/out", who);
+  if (dtype != FA_BF16 && dtype != FA_F16)
+    return fail(dtype == FA_F32 ? FA_EUNSUPPORTED : FA_EINVAL, "%s: dtype %d (bf16 or f16)", who, dtype);
+  if (in_features <= 0 || in_features % 8 != 0)
+    return fail(FA_EINVAL, "%s: in_features %d must be a positive multiple of 8", who, in_features);
+  if (out_features <= 0 || out_features % 32 != 0)
+    return fail(FA_EINVAL, "%s: out_features %d must be a positive multiple of 32", who, out_features);
+  if (!aligned(attn, 16) || !aligned(weight, 16) || !aligned(out, 32) ||
+      (residual && !aligned(residual, 16)))
+    return fail(FA_EINVAL, "%s: misaligned attn/weight/residual (16 B) or out (32 B)", who);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == FA_BF16) {
+    fa::ResidualEpilogue<__nv_bfloat16> epi{static_cast<__nv_bfloat16 *>(out),
+                                            static_cast<const __nv_bfloat16 *>(residual)};
+    return launch_gemm<__nv_bfloat16>(num_tokens, out_features, in_features, epi, attn, weight,
+                                      dtype, st, who);
+  }
+  fa::ResidualEpilogue<__half> epi{static_cast<__half *>(out), static_cast<const __half *>(residual)};
+  return launch_gemm<__half>(num_tokens, out_features, in_features, epi, attn, weight, dtype, st, who);
+}
+
 }  // extern "C"
+

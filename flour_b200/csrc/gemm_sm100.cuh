@@ -1,0 +1,329 @@
+// Projection GEMMs around the attention call, on the 5th-generation tensor cores (tcgen05), with
+// the work that follows each GEMM fused into its epilogue:
+//
+//   QKV:    [q | k | v] = x W^T (+ bias), per-head RMSNorm of q and k (optional), rotate-half
+//           RoPE of q and k, q written token-major, k and v scattered straight into the paged
+//           pool through slot_mapping. Replaces q/k/v_proj, q/k_norm, rope and write_kv of
+//           CausalSelfAttention::forward (src/models/common/attention.rs:75-104).
+//   o_proj: out = residual + attn W_o^T. Replaces o_proj (attention.rs:116) and the residual add
+//           of DecoderLayer::forward (src/models/common/transformer.rs:37-38).
+//
+// GEMM: C[M, N] = A[M, K] B[N, K]^T, both operands K-major (row-major activations and
+// (out, in) weights, as candle's Linear stores them). Persistent: one CTA per SM walks output
+// tiles of 128 x BN. Warp 0 streams 128 x 64 A and BN x 64 B tiles by TMA (128-byte swizzle)
+// through a kStages ring; warp 1 issues tcgen05.mma (M=128, N=BN, K=16, both operands in shared
+// memory) into one of two TMEM accumulators; warps 2-5 (thread = output row) run the epilogue of
+// tile i while the MMAs of tile i+1 accumulate into the other buffer.
+//
+// Every mbarrier wait is bounded; bad device data (slots, positions) sets a status bit and the
+// affected row is skipped.
+#pragma once
+
+#include "tcgen05.cuh"
+
+namespace fa {
+
+constexpr int kGemmBK = 64;          // K per ring stage: one 128-byte swizzled row per operand row
+constexpr int kGemmThreads = 192;    // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
+
+template <int BN>
+struct GemmCfg {
+  static_assert(BN == 128 || BN == 256, "BN is 128 or 256");
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = 128 * kGemmBK * 2;
+  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int FULL = 0, EMPTY = kStages, AFULL = 2 * kStages, AEMPTY = AFULL + 2,
+                       DRAIN = AEMPTY + 2, NBARS = DRAIN + 1;
+  static constexpr int kBarOff = kStages * kStageBytes;
+  static constexpr int kMiscOff = kBarOff + NBARS * 8;
+  static constexpr int kBytes = kMiscOff + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+};
+
+struct GemmShape {
+  int32_t M, N, K;
+  int32_t tiles_m, tiles_n;
+};
+
+// ---- epilogues (called by each epilogue thread for its row of one output tile) -------------
+
+// Load 32 consecutive f32 accumulator columns of this thread's row.
+__device__ __forceinline__ void acc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tc::ld32(taddr, r);
+  tc::wait_ld();
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(x);
+  else return __half2float(x);
+}
+
+// 32 values -> 16 packed pairs -> two 256-bit stores.
+template <typename T>
+__device__ __forceinline__ void store32(T *dst, const float (&v)[32]) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) pk[e] = pack2<T>(v[2 * e], v[2 * e + 1]);
+  st_global_v8(dst, pk);
+  st_global_v8(dst + 16, pk + 8);
+}
+
+template <typename T>
+struct QkvEpilogue {
+  T *q_out;                 // [M, num_heads, head_dim]
+  T *k_cache, *v_cache;     // [num_blocks, num_kv_heads, block_size, head_dim]
+  const T *bias;            // [N] or null
+  const T *q_norm, *k_norm; // [head_dim] or null
+  const float *rope_cos, *rope_sin;  // [max_position, head_dim / 2]
+  const int32_t *positions, *slots;  // [M]
+  float rms_eps;
+  int32_t num_heads, num_kv_heads, head_dim, num_blocks, block_size, max_position;
+
+  // One row (token) of a 128 x BN tile: BN / head_dim whole heads starting at column col0.
+  template <int BN>
+  __device__ void operator()(uint32_t tacc, int row, int col0, const GemmShape &s) const {
+    const bool row_ok = row < s.M;
+    const int half = head_dim / 2;
+    int pos = 0, slot = -1;
+    if (row_ok) {
+      pos = positions[row];
+      slot = slots[row];
+    }
+    for (int hl = 0; hl < BN / head_dim; ++hl) {
+      const int f0 = col0 + hl * head_dim;  // warp-uniform
+      if (f0 >= s.N) break;
+      const int gh = f0 / head_dim;
+      const bool is_q = gh < num_heads, is_k = !is_q && gh < num_heads + num_kv_heads;
+      const T *nw = is_q ? q_norm : (is_k ? k_norm : nullptr);
+      const uint32_t ta = tacc + hl * head_dim;
+      // Destination row, or null when this row writes nothing for this head.
+      T *dst = nullptr;
+      bool rope_ok = true;
+      if (row_ok && (is_q || is_k)) {
+        rope_ok = pos >= 0 && pos < max_position;
+        if (!rope_ok) report(FA_DEVERR_POSITION);
+      }
+      if (row_ok && rope_ok) {
+        if (is_q) {
+          dst = q_out + (size_t(row) * num_heads + gh) * head_dim;
+        } else if (slot >= 0) {
+          const int blk = slot / block_size, off = slot % block_size;
+          if (blk < num_blocks) {
+            const int kvh = gh - num_heads - (is_k ? 0 : num_kv_heads);
+            dst = (is_k ? k_cache : v_cache) +
+                  ((size_t(blk) * num_kv_heads + kvh) * block_size + off) * head_dim;
+          } else {
+            report(FA_DEVERR_SLOT);
+          }
+        } else if (slot < -1) {
+          report(FA_DEVERR_SLOT);
+        }
+      }
+      // RMSNorm over the head (after the bias, before RoPE: attention.rs:85-99).
+      float inv_rms = 1.f;
+      if (nw) {
+        float ss = 0.f;
+        for (int c = 0; c < head_dim / 32; ++c) {
+          float v[32];
+          acc_ld32(ta + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = v[e] + (bias ? to_f32(bias[f0 + c * 32 + e]) : 0.f);
+            ss = fmaf(x, x, ss);
+          }
+        }
+        inv_rms = rsqrtf(ss / float(head_dim) + rms_eps);
+      }
+      // Rotate-half RoPE pairs column i with column i + head_dim/2 (i < head_dim/2).
+      for (int c = 0; c < half / 32; ++c) {
+        float a[32], b[32];
+        acc_ld32(ta + c * 32, a);
+        acc_ld32(ta + half + c * 32, b);
+        if (dst == nullptr) continue;
+        const int i0 = c * 32;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (bias) {
+            a[e] += to_f32(bias[f0 + i0 + e]);
+            b[e] += to_f32(bias[f0 + half + i0 + e]);
+          }
+          if (nw) {
+            a[e] *= inv_rms * to_f32(nw[i0 + e]);
+            b[e] *= inv_rms * to_f32(nw[half + i0 + e]);
+          }
+        }
+        if (is_q || is_k) {
+          const float4 *cp = reinterpret_cast<const float4 *>(rope_cos + size_t(pos) * half + i0);
+          const float4 *sp = reinterpret_cast<const float4 *>(rope_sin + size_t(pos) * half + i0);
+#pragma unroll
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 c4 = cp[e4], s4 = sp[e4];
+            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int e = e4 * 4 + j;
+              const float x1 = a[e], x2 = b[e];
+              a[e] = x1 * cs[j] - x2 * sn[j];
+              b[e] = x2 * cs[j] + x1 * sn[j];
+            }
+          }
+        }
+        store32<T>(dst + i0, a);
+        store32<T>(dst + half + i0, b);
+      }
+    }
+  }
+};
+
+template <typename T>
+struct ResidualEpilogue {
+  T *out;                 // [M, N]
+  const T *residual;      // [M, N] or null
+
+  template <int BN>
+  __device__ void operator()(uint32_t tacc, int row, int col0, const GemmShape &s) const {
+    const bool row_ok = row < s.M;
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = col0 + c * 32;  // warp-uniform
+      if (col >= s.N) break;
+      float v[32];
+      acc_ld32(tacc + c * 32, v);
+      if (!row_ok) continue;
+      const size_t base = size_t(row) * s.N + col;
+      if (residual) {
+        const uint4 *rp = reinterpret_cast<const uint4 *>(residual + base);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = rp[q];
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<T>(ww[j]);
+            v[q * 8 + 2 * j] += f.x;
+            v[q * 8 + 2 * j + 1] += f.y;
+          }
+        }
+      }
+      store32<T>(out + base, v);
+    }
+  }
+};
+
+// ---- the persistent GEMM ---------------------------------------------------------------------
+
+template <typename T, int BN, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ GemmShape s, const __grid_constant__ Epi epi,
+                   const __grid_constant__ CUtensorMap tm_a,
+                   const __grid_constant__ CUtensorMap tm_b) {
+  using C = GemmCfg<BN>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tiles = s.tiles_m * s.tiles_n;
+  const int num_k = (s.K + kGemmBK - 1) / kGemmBK;
+
+  if (tid == 0) {
+    for (int i = 0; i < C::NBARS; ++i)
+      mbar_init(bar(i), (i == C::AEMPTY || i == C::AEMPTY + 1) ? 128 : 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::alloc(smem_u32(s_tmem), C::kTmemCols);
+    tc::relinquish();
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m = t / s.tiles_n, n = t % s.tiles_n;
+        for (int kb = 0; kb < num_k; ++kb, ++it) {
+          const int st = it % C::kStages;
+          if (it >= C::kStages && !(ok = mbar_wait(bar(C::EMPTY + st), ((it / C::kStages) - 1) & 1)))
+            break;
+          mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
+          const uint32_t a = sbase + st * C::kStageBytes;
+          tma_load_2d(a, &tm_a, bar(C::FULL + st), kb * kGemmBK, m * 128);
+          tma_load_2d(a + C::kABytes, &tm_b, bar(C::FULL + st), kb * kGemmBK, n * BN);
+        }
+      }
+      if (!ok) report(FA_DEVERR_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(kBf16, 128, BN, false, false);
+      int it = 0, tc_n = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc_n) {
+        const int buf = tc_n & 1;
+        if (tc_n >= 2 && !(ok = mbar_wait(bar(C::AEMPTY + buf), ((tc_n >> 1) - 1) & 1))) break;
+        tc::fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < num_k; ++kb, ++it) {
+          const int st = it % C::kStages;
+          if (!(ok = mbar_wait(bar(C::FULL + st), (it / C::kStages) & 1))) break;
+          tc::fence_after();
+          const uint32_t a = sbase + st * C::kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk)
+            tc::mma_ss(d, tc::sw128_desc(a + kk * 32, 16, 1024),
+                       tc::sw128_desc(a + C::kABytes + kk * 32, 16, 1024), idesc,
+                       (kb > 0 || kk > 0) ? 1u : 0u);
+          tc::commit(bar(C::EMPTY + st));
+        }
+        if (!ok) break;
+        tc::commit(bar(C::AFULL + buf));
+      }
+      if (!ok) report(FA_DEVERR_TIMEOUT);
+      tc::commit(bar(C::DRAIN));  // every MMA issued above has completed once this arrives
+      mbar_wait(bar(C::DRAIN), 0);
+    }
+  } else {
+    // ================= epilogue: thread = output row of the tile =================
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const uint32_t lane_off = uint32_t(q * 32) << 16;
+    int tc_n = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc_n) {
+      const int buf = tc_n & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(C::AFULL + buf), (tc_n >> 1) & 1))) {
+        if (lane == 0) report(FA_DEVERR_TIMEOUT);
+        break;
+      }
+      tc::fence_after();
+      const int m = t / s.tiles_n, n = t % s.tiles_n;
+      epi.template operator()<BN>(tmem + lane_off + buf * BN, m * 128 + q * 32 + lane, n * BN, s);
+      tc::fence_before();
+      mbar_arrive(bar(C::AEMPTY + buf));
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::dealloc(tmem, C::kTmemCols);
+  }
+}
+
+}  // namespace fa

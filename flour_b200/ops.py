@@ -205,3 +205,77 @@ def device_status(clear: bool = True, stream=None) -> int:
 def default_scale(head_dim: int) -> float:
     """1/sqrt(head_dim), the scale attention.rs:108 passes."""
     return 1.0 / math.sqrt(head_dim)
+
+
+# ---- the projections either side of attention (CausalSelfAttention::forward) --------------
+
+def _c16(t: torch.Tensor | None, name: str, dtype: torch.dtype) -> torch.Tensor | None:
+    if t is None:
+        return None
+    if t.dtype != dtype or not t.is_contiguous() or not t.is_cuda:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"{name} must be a contiguous CUDA {dtype} tensor")
+    return t
+
+
+def qkv_rope_cache(x, weight, k_cache, v_cache, positions, slot_mapping, num_heads: int,
+                   rope_cos, rope_sin, bias=None, q_norm_weight=None, k_norm_weight=None,
+                   rms_eps: float = 1e-6, q_out=None, stream=None) -> torch.Tensor:
+    """Fused q/k/v projection + (optional) per-head RMSNorm + RoPE + reshape_and_cache.
+
+    x [T, hidden]; weight [(num_heads + 2*kv_heads) * d, hidden] (q_proj, k_proj, v_proj rows
+    stacked); positions / slot_mapping int32 [T]; rope_cos / rope_sin f32 [max_position, d/2].
+    Returns q [T, num_heads, d]; K/V land in the pool. attention.rs:75-104."""
+    layer = layer_desc(k_cache, v_cache)
+    dt = k_cache.dtype
+    x = _c16(x, "x", dt)
+    weight = _c16(weight, "weight", dt)
+    for name, t in (("bias", bias), ("q_norm_weight", q_norm_weight), ("k_norm_weight", k_norm_weight)):
+        _c16(t, name, dt)
+    if rope_cos.dtype != torch.float32 or rope_sin.dtype != torch.float32 or \
+            not (rope_cos.is_contiguous() and rope_sin.is_contiguous()) or rope_cos.shape != rope_sin.shape:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "rope tables must be contiguous f32 [max_pos, d/2]")
+    T, hidden = x.shape
+    d = k_cache.shape[-1]
+    n_out = (num_heads + 2 * k_cache.shape[1]) * d
+    if tuple(weight.shape) != (n_out, hidden) or (bias is not None and tuple(bias.shape) != (n_out,)):
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"weight must be [{n_out}, {hidden}] (bias [{n_out}])")
+    for name, t in (("q_norm_weight", q_norm_weight), ("k_norm_weight", k_norm_weight)):
+        if t is not None and tuple(t.shape) != (d,):
+            raise _lib.FlourAttnError(_lib.FA_EINVAL, f"{name} must be [{d}]")
+    if rope_cos.dim() != 2 or rope_cos.shape[1] != d // 2:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"rope tables must be [max_pos, {d // 2}]")
+    if q_out is None:
+        q_out = torch.empty((T, num_heads, d), dtype=dt, device=x.device)
+    w = _lib.FaQkvWeights(weight.data_ptr(), bias.data_ptr() if bias is not None else None,
+                          q_norm_weight.data_ptr() if q_norm_weight is not None else None,
+                          k_norm_weight.data_ptr() if k_norm_weight is not None else None,
+                          float(rms_eps), hidden, num_heads, rope_cos.data_ptr(),
+                          rope_sin.data_ptr(), rope_cos.shape[0])
+    check(lib().fa_qkv_rope_cache(ctypes.byref(layer), ctypes.byref(w), _ptr(x),
+                                  _ptr(_i32(positions, "positions")),
+                                  _ptr(_i32(slot_mapping, "slot_mapping")), T, _ptr(q_out),
+                                  _stream(stream)),
+          "qkv_rope_cache")
+    return q_out
+
+
+def o_proj_residual(attn, weight, residual=None, out=None, stream=None) -> torch.Tensor:
+    """out = residual + attn @ weight^T (residual optional, may alias out).
+
+    attn [T, in_features] (heads concatenated), weight [out_features, in_features].
+    attention.rs:116 + transformer.rs:37-38."""
+    dt = attn.dtype
+    attn = _c16(attn, "attn", dt)
+    weight = _c16(weight, "weight", dt)
+    _c16(residual, "residual", dt)
+    T, fin = attn.shape
+    fout = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != fin or \
+            (residual is not None and tuple(residual.shape) != (T, fout)):
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "weight must be [out, in], residual [T, out]")
+    if out is None:
+        out = torch.empty((T, fout), dtype=dt, device=attn.device)
+    check(lib().fa_o_proj_residual(_ptr(attn), _ptr(weight), _ptr(residual), _ptr(out), T, fin,
+                                   fout, fa_dtype(dt), _stream(stream)),
+          "o_proj_residual")
+    return out

@@ -303,3 +303,22 @@ def build_batch(tables: list[BlockTable], q_lens: list[int], device) -> BatchMet
     return BatchMetadata(bt.to(device), ctx.to(device), cu.to(device),
                          torch.tensor(slots, dtype=torch.int32).to(device),
                          int(ctx.max()) if B else 0, max(q_lens) if q_lens else 0)
+
+
+def rope_tables(head_dim: int, max_position: int, rope_theta: float, dtype: torch.dtype,
+                device=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The RoPE tables of Cache::new (cache.rs:378-392), as the f32 tensors the fused QKV
+    kernel reads: theta_i = 1 / rope_theta^(2i / head_dim) and angle = position * theta_i in
+    f32, then cos/sin rounded to the model dtype exactly as the reference stores them.
+
+    Host-side setup done once per model; returns (cos, sin), each [max_position, head_dim/2]."""
+    half = head_dim // 2
+    i = torch.arange(half, dtype=torch.float32)
+    theta = 1.0 / torch.pow(torch.tensor(rope_theta, dtype=torch.float32), (2 * i) / head_dim)
+    pos = torch.arange(max_position, dtype=torch.float32).reshape(-1, 1)
+    ang = pos * theta.reshape(1, half)
+    cos = ang.cos().to(dtype).to(torch.float32).contiguous()
+    sin = ang.sin().to(dtype).to(torch.float32).contiguous()
+    if device is not None:
+        cos, sin = cos.to(device), sin.to(device)
+    return cos, sin

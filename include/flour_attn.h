@@ -72,6 +72,7 @@ typedef enum fa_dtype { FA_F32 = 0, FA_BF16 = 1, FA_F16 = 2 } fa_dtype;
 #define FA_DEVERR_TIMEOUT 0x8    /* a bounded wait on an mbarrier gave up */
 #define FA_DEVERR_SEQLEN 0x10    /* cu_seqlens_q not non-decreasing or past total_q */
 #define FA_DEVERR_PAIR 0x20      /* copy_blocks pair entry outside [0, num_blocks) */
+#define FA_DEVERR_POSITION 0x40  /* RoPE position outside [0, max_position) */
 
 /* One layer of the paged KV pool. */
 typedef struct fa_kv_layer {
@@ -198,6 +199,50 @@ FA_API fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, v
                            int32_t num_seqs, int32_t num_heads, int32_t n_rep, int32_t total_q,
                            int32_t max_seqlen_q, int32_t max_context_len, float scale,
                            void *workspace, size_t workspace_bytes, fa_stream_t stream);
+
+/* ---- the steps either side of attention (CausalSelfAttention::forward) ----------------- */
+
+/* Weights of one layer's q/k/v projections, as candle's Linear stores them (out, in). */
+typedef struct fa_qkv_weights {
+  const void *weight;         /* device [(num_heads + 2*num_kv_heads) * head_dim, hidden]: the
+                                 q_proj, k_proj, v_proj weights stacked in that order; pool dtype */
+  const void *bias;           /* device [(num_heads + 2*num_kv_heads) * head_dim] or NULL
+                                 (use_qkv_bias, attention.rs:28-33) */
+  const void *q_norm_weight;  /* device [head_dim] or NULL: RMSNorm per query head (use_qk_norm) */
+  const void *k_norm_weight;  /* device [head_dim] or NULL: RMSNorm per key head */
+  float rms_eps;
+  int32_t hidden;
+  int32_t num_heads;
+  const float *rope_cos;      /* device f32 [max_position, head_dim/2]: Cache::new's cos table */
+  const float *rope_sin;      /* (src/models/common/cache.rs:378-392), 16-byte aligned */
+  int32_t max_position;
+} fa_qkv_weights;
+
+/* Fused QKV projection + RoPE + reshape_and_cache. For each token t of x [num_tokens, hidden]:
+ *   q|k|v = x[t] W^T (+ bias); q, k -> RMSNorm per head when a norm weight is given;
+ *   q, k  -> rotate-half RoPE at positions[t] (candle_nn::rotary_emb::rope with the tables above);
+ *   q     -> q_out[t] ([num_tokens, num_heads, head_dim]);
+ *   k, v  -> the pool slot slot_mapping[t] (-1 skips the token), like fa_reshape_and_cache.
+ * Replaces q/k/v_proj, q/k_norm, rope and Cache::write_kv of CausalSelfAttention::forward
+ * (src/models/common/attention.rs:75-104). Computes in f32 and rounds each output once.
+ * Requires a 16-bit pool, head_dim 64 or 128, hidden % 8 == 0, 16-byte aligned x and weight,
+ * 32-byte aligned q_out. Bad positions / slots in device memory set FA_DEVERR_POSITION /
+ * FA_DEVERR_SLOT and skip the row. */
+FA_API fa_status fa_qkv_rope_cache(const fa_kv_layer *layer, const fa_qkv_weights *weights,
+                                   const void *x, const int32_t *positions,
+                                   const int32_t *slot_mapping, int32_t num_tokens, void *q_out,
+                                   fa_stream_t stream);
+
+/* Fused output projection + residual: out[t] = residual[t] + attn[t] W_o^T, with attn
+ * [num_tokens, in_features] (the attention output, heads concatenated), weight
+ * [out_features, in_features] and residual / out [num_tokens, out_features]; residual may be
+ * NULL (plain projection) and may alias out. Replaces o_proj (attention.rs:116) and the residual
+ * add of DecoderLayer::forward (src/models/common/transformer.rs:37-38).
+ * Requires dtype FA_BF16 or FA_F16, in_features % 8 == 0, out_features % 32 == 0, 16-byte
+ * aligned attn / weight / residual and 32-byte aligned out. */
+FA_API fa_status fa_o_proj_residual(const void *attn, const void *weight, const void *residual,
+                                    void *out, int32_t num_tokens, int32_t in_features,
+                                    int32_t out_features, int32_t dtype, fa_stream_t stream);
 
 #ifdef __cplusplus
 }
