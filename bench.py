@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-longctx", action="store_true")
+    ap.add_argument("--no-projections", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -336,6 +337,12 @@ def run_ours(args):
         longctx = run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks,
                               barrier, world)
 
+    # ---- the fused projections either side of attention ---------------------------------------
+    proj = None
+    if not args.no_projections:
+        proj = run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_ranks,
+                               barrier)
+
     # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------------
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
@@ -377,6 +384,8 @@ def run_ours(args):
             line["prefill"] = prefill
         if longctx:
             line["longctx"] = longctx
+        if proj:
+            line["projections"] = proj
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
@@ -560,6 +569,55 @@ def run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks, b
            "pool_gb": round(nb * block_bytes / 1e9, 1), "mean_ctx": float(np.mean(ctx))}
     del b, out, ws
     torch.cuda.empty_cache()
+    return res
+
+
+def run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_ranks, barrier):
+    """Llama-3-8B layer projections through the fused kernels: QKV + RoPE + reshape_and_cache
+    (hidden 4096 -> 48 heads x 128) and o_proj + residual (4096 -> 4096), at the C3 prefill
+    token count and at the C2 decode batch (64 tokens)."""
+    from flour_b200.paged import rope_tables
+    hidden, Hq, Hkv, d = 4096, 32, 8, 128
+    N = (Hq + 2 * Hkv) * d
+    g = torch.Generator(device=dev).manual_seed(seed + 7)
+    w = (torch.randn(N, hidden, device=dev, generator=g) / 64).to(torch.bfloat16)
+    wo = (torch.randn(hidden, Hq * d, device=dev, generator=g) / 64).to(torch.bfloat16)
+    cos, sin = rope_tables(d, 8192, 500000.0, torch.bfloat16, dev)
+    res = {}
+    for name, T in (("prefill_c3_tokens", 15401), ("decode_c2_batch", 64)):
+        x = torch.randn(T, hidden, device=dev, generator=g).to(torch.bfloat16)
+        a = torch.randn(T, Hq * d, device=dev, generator=g).to(torch.bfloat16)
+        nb = T // 16 + 8
+        kc = torch.zeros(nb, Hkv, 16, d, device=dev, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        pos = torch.arange(T, dtype=torch.int32, device=dev) % 8192
+        slots = torch.arange(T, dtype=torch.int32, device=dev)
+        q = torch.empty(T, Hq, d, device=dev, dtype=torch.bfloat16)
+        out = torch.empty(T, hidden, device=dev, dtype=torch.bfloat16)
+        fns = {"qkv_rope_cache": lambda: ops.qkv_rope_cache(x, w, kc, vc, pos, slots, Hq, cos, sin,
+                                                            q_out=q),
+               "o_proj_residual": lambda: ops.o_proj_residual(a, wo, x, out=out)}
+        flops = {"qkv_rope_cache": 2 * T * hidden * N, "o_proj_residual": 2 * T * Hq * d * hidden}
+        wbytes = {"qkv_rope_cache": N * hidden * 2, "o_proj_residual": hidden * Hq * d * 2}
+        entry = {"tokens": T}
+        for k, fn in fns.items():
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 20
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+            entry[k] = {"ms": round(ms, 4), "tflops": round(flops[k] / ms / 1e9, 1),
+                        "frac_of_measured_tensor_peak": round(flops[k] / ms / 1e9 / tc_peak, 4),
+                        "weight_gbps": round(wbytes[k] / ms / 1e6, 1)}
+        res[name] = entry
+    assert ops.device_status() == 0
     return res
 
 

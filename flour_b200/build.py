@@ -19,6 +19,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
+HOST = PKG / "host"
 LIB = PKG / "libflour_attn.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -31,7 +32,8 @@ def nvcc() -> str:
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "flour_attn.h"]
+    return (sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(HOST.glob("*.cpp")) +
+            sorted(HOST.glob("*.h")) + [ROOT / "include" / "flour_attn.h"])
 
 
 def needs_build() -> bool:
@@ -51,10 +53,10 @@ def build(verbose: bool = False, force: bool = False, out: Path | None = None,
     cmd = [
         nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
         "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
-        "-I", str(ROOT / "include"), "-I", str(CSRC),
+        "-I", str(ROOT / "include"), "-I", str(CSRC), "-I", str(HOST),
         "-cudart", "static",
         *[f"-D{d}" for d in defines],
-        "-o", str(target), str(CSRC / "flour_attn.cu"),
+        "-o", str(target), str(CSRC / "flour_attn.cu"), str(HOST / "flour_host.cpp"),
     ]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
