@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-longctx", action="store_true")
     ap.add_argument("--no-projections", action="store_true")
+    ap.add_argument("--no-c5", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -331,6 +332,12 @@ def run_ours(args):
         prefill = run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_ranks,
                               barrier, world)
 
+    # ---- C5 mixed serving step, strong-scaled over the ranks ---------------------------------
+    c5 = None
+    if not args.no_c5:
+        c5 = run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier)
+        torch.cuda.empty_cache()  # return C5's pools before C4 sizes its pool from free memory
+
     # ---- long-context split-K decode (C4) ----------------------------------------------------
     longctx = None
     if not args.no_longctx:
@@ -386,6 +393,8 @@ def run_ours(args):
             line["longctx"] = longctx
         if proj:
             line["projections"] = proj
+        if c5:
+            line["c5"] = c5
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
@@ -569,6 +578,79 @@ def run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks, b
            "pool_gb": round(nb * block_bytes / 1e9, 1), "mean_ctx": float(np.mean(ctx))}
     del b, out, ws
     torch.cuda.empty_cache()
+    return res
+
+
+def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
+    """C5 mixed serving step: Qwen2-7B heads (Hq=28, Hkv=4, d=128), 28 layers, 512 sequences
+    (ctx ~ LogNormal(ln 1024, 0.8) capped at 8192); about 10 % are new prompts of L ~ U[256, 2048]
+    run as prefill, the rest decode one token. The sequences are partitioned longest-first over
+    the ranks, so the total work is fixed as N grows (strong scaling). One step = per layer:
+    reshape_and_cache of the new K/V, the decode launch and the prefill launch; each rank owns its
+    own pools. KV values are zero-filled (timing only; the kernels' arithmetic does not depend on
+    the values)."""
+    from flour_b200.workloads import QWEN7B, c5_plan, lpt_partition, make_decode, make_prefill
+    h, L = QWEN7B, 28
+    ctx, is_pf, pf_len, cost = c5_plan(args.seed)
+    mine = lpt_partition(cost, world)[rank]
+    dec = [i for i in mine if not is_pf[i]]
+    pf = [i for i in mine if is_pf[i]]
+    scale = 1.0 / math.sqrt(h.head_dim)
+    db = make_decode(h, ctx[dec], torch.bfloat16, dev, args.seed + rank, num_layers=L, fill=False)
+    for t in db.k_caches + db.v_caches:
+        t.zero_()
+    B = len(dec)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 11)
+    dq = torch.randn((B, h.num_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
+    dk = torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
+    dv = torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
+    bt = db.block_tables.cpu().numpy()
+    last = db.ctx_host.astype(np.int64) - 1
+    dslots = torch.tensor(bt[np.arange(B), last // 16] * 16 + last % 16, dtype=torch.int32, device=dev)
+    dout = torch.empty_like(dq)
+    pb = make_prefill(h, pf_len[pf], np.zeros(len(pf), np.int64), torch.bfloat16, dev,
+                      args.seed + 100 + rank, num_layers=L, fill=False) if pf else None
+    pout = torch.empty_like(pb.q) if pb is not None else None
+    ws_d, ws_p = ops.Workspace(dev), ops.Workspace(dev)
+    ws_d.get(ops.workspace_size(B, h.num_heads, h.num_kv_heads, h.head_dim, db.max_context_len, 1))
+
+    def step():
+        for l in range(L):
+            ops.reshape_and_cache(db.k_caches[l], db.v_caches[l], dk, dv, dslots)
+            ops.paged_decode(dq, db.k_caches[l], db.v_caches[l], db.block_tables, db.context_lens,
+                             h.n_rep, scale, db.max_context_len, ws_d, out=dout)
+            if pb is not None:
+                ops.reshape_and_cache(pb.k_caches[l], pb.v_caches[l], pb.key, pb.value,
+                                      pb.slot_mapping)
+                ops.paged_prefill(pb.q, pb.k_caches[l], pb.v_caches[l], pb.cu_seqlens_q,
+                                  pb.context_lens, pb.block_tables, h.n_rep, scale,
+                                  pb.max_seqlen_q, pb.max_context_len, ws_p, out=pout)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    barrier()
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+    kvb = h.num_kv_heads * h.head_dim * 2 * 2
+    dec_bytes = float(ctx[~is_pf].sum()) * kvb * L
+    pf_flops = float((4.0 * h.num_heads * h.head_dim * pf_len[is_pf] * (pf_len[is_pf] + 1) / 2).sum()) * L
+    tokens = int((~is_pf).sum() + pf_len[is_pf].sum())
+    res = {"config": "C5 mixed serving step: Qwen2-7B heads, 28 layers, 512 seqs (ctx ~ LogNormal"
+                     "(ln 1024, 0.8) <= 8192), ~10 % new prefills L ~ U[256, 2048]; LPT over ranks",
+           "scaling": "strong", "step_ms": round(ms, 4),
+           "tokens_per_s": round(tokens / (ms / 1e3), 1),
+           "decode_seqs": int((~is_pf).sum()), "prefill_seqs": int(is_pf.sum()),
+           "prefill_tokens": int(pf_len[is_pf].sum()),
+           "decode_kv_gb_per_step": round(dec_bytes / 1e9, 3),
+           "prefill_tflop_per_step": round(pf_flops / 1e12, 3)}
     return res
 
 

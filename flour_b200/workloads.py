@@ -215,6 +215,67 @@ def make_c3(device, seed: int = 3, dtype=torch.bfloat16, num_layers: int = 1,
                         lens.astype(np.int64), prefix, int(suffix.max()), int(lens.max()), total)
 
 
+def make_prefill(heads: Heads, lens, prefix, dtype: torch.dtype, device, seed: int,
+                 num_layers: int = 1, fill: bool = True) -> PrefillBatch:
+    """A packed prefill batch: sequence i holds lens[i] tokens, the first prefix[i] of them
+    already cached; every sequence owns private, randomly placed blocks of one pool. With
+    fill=False the pools, queries and new K/V are zero-filled instead of random (timing runs)."""
+    rng = np.random.default_rng(seed)
+    bs = heads.block_size
+    lens = np.asarray(lens, dtype=np.int64)
+    prefix = np.asarray(prefix, dtype=np.int64)
+    pages = (lens + bs - 1) // bs
+    total = max(1, int(pages.sum()))
+    perm = rng.permutation(total).astype(np.int32)
+    max_blocks = max(1, int(pages.max()) if len(lens) else 1)
+    bt = np.zeros((len(lens), max_blocks), dtype=np.int32)
+    o = 0
+    for i, n in enumerate(pages):
+        bt[i, :n] = perm[o:o + n]
+        o += int(n)
+    suffix = lens - prefix
+    cu = np.concatenate([[0], np.cumsum(suffix)]).astype(np.int32)
+    slots = np.concatenate([bt[i, np.arange(prefix[i], lens[i]) // bs] * bs +
+                            np.arange(prefix[i], lens[i]) % bs for i in range(len(lens))]
+                           ) if len(lens) else np.zeros(0, np.int64)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    make = (lambda shape: _randn(shape, dtype, device, gen)) if fill else \
+        (lambda shape: torch.zeros(shape, dtype=dtype, device=device))
+    shape = (total, heads.num_kv_heads, bs, heads.head_dim)
+    kc = [make(shape) for _ in range(num_layers)]
+    vc = [make(shape) for _ in range(num_layers)]
+    tq = int(cu[-1])
+    q = make((tq, heads.num_heads, heads.head_dim))
+    key = make((tq, heads.num_kv_heads, heads.head_dim))
+    value = make((tq, heads.num_kv_heads, heads.head_dim))
+    return PrefillBatch(heads, dtype, q, key, value, kc, vc,
+                        torch.from_numpy(cu).to(device),
+                        torch.from_numpy(lens.astype(np.int32)).to(device),
+                        torch.from_numpy(bt).to(device),
+                        torch.from_numpy(slots.astype(np.int32)).to(device),
+                        lens, prefix, int(suffix.max()) if len(lens) else 0,
+                        int(lens.max()) if len(lens) else 0, total)
+
+
+def c5_plan(seed: int, n: int = 512, prefill_frac: float = 0.1):
+    """C5 mixed serving step (Qwen2-7B heads): 512 sequences with ctx ~ LogNormal(ln 1024, 0.8)
+    capped at 8192; a prefill_frac share are new prompts of L ~ U[256, 2048] (no cached prefix),
+    the rest decode one token. Returns (ctx, is_prefill, prefill_len, cost) where cost is an
+    estimated time per sequence (decode: KV bytes at HBM speed; prefill: causal FLOPs at tensor
+    speed) for longest-first partitioning across GPUs."""
+    rng = np.random.default_rng(seed + 55)
+    ctx = c5_contexts(seed, n)
+    is_pf = rng.random(n) < prefill_frac
+    pf_len = rng.integers(256, 2049, size=n)
+    h = QWEN7B
+    kv_bytes_per_token = h.num_kv_heads * h.head_dim * 2 * 2
+    dec_cost = ctx * kv_bytes_per_token / 6.4e12
+    pf_cost = 4.0 * h.num_heads * h.head_dim * pf_len * (pf_len + 1) / 2 / 7.0e14 + \
+        pf_len * kv_bytes_per_token / 6.4e12
+    return ctx, is_pf, pf_len, np.where(is_pf, pf_cost, dec_cost)
+
+
 def lpt_partition(costs, parts: int) -> list[list[int]]:
     """Longest-processing-time-first assignment of items to `parts` bins (sequence sharding)."""
     order = np.argsort(-np.asarray(costs, dtype=np.float64), kind="stable")
