@@ -421,9 +421,53 @@ fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, cons
   return check_launch(who);
 }
 
+// Split-K over a cluster of `ranks` CTAs per 128 x 128 tile (one tile per cluster).
+template <typename T, class Epi>
+fa_status launch_gemm_splitk(int M, int N, int K, int ranks, const Epi &epi, const void *a,
+                             const void *b, int32_t dt, cudaStream_t stream, const char *who) {
+  constexpr int BN = 128;
+  using C = fa::GemmCfg<BN>;
+  fa::GemmShape s{M, N, K, (M + 127) / 128, (N + BN - 1) / BN};
+  CUtensorMap ta, tb;
+  if (fa_status st = make_gemm_map(&ta, a, M, K, dt, 128, who); st != FA_OK) return st;
+  if (fa_status st = make_gemm_map(&tb, b, N, K, dt, BN, who); st != FA_OK) return st;
+  auto kern = fa::gemm_tn_splitk_kernel<T, BN, Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: set smem attribute: %s", who, cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(s.tiles_m * s.tiles_n * ranks));
+  cfg.blockDim = dim3(fa::kGemmThreads);
+  cfg.dynamicSmemBytes = C::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(ranks);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, s, epi, ta, tb);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: cluster launch: %s", who, cudaGetErrorString(e));
+  return check_launch(who);
+}
+
+// How many CTAs split K when 128-wide tiles leave most SMs idle (1 = no split). Clusters need
+// their CTAs inside one GPC; measured on B200 (64 tokens, Llama-3-8B projections), splits that
+// keep the grid near 2/3 of the SMs schedule in one wave, larger ones spill into a second.
+int gemm_split_ranks(int M, int N, int K) {
+  const int64_t tiles = int64_t((M + 127) / 128) * ((N + 127) / 128);
+  const int num_k = (K + fa::kGemmBK - 1) / fa::kGemmBK;
+  const int64_t target = std::max(1, sm_count() * 2 / 3);
+  int r = int(std::min<int64_t>(fa::kSplitMaxRanks, target / std::max<int64_t>(1, tiles)));
+  r = std::min(r, num_k / 4);  // at least 4 K blocks per CTA
+  return r >= 2 ? r : 1;
+}
+
 template <typename T, class Epi>
 fa_status launch_gemm(int M, int N, int K, const Epi &epi, const void *a, const void *b,
                       int32_t dt, cudaStream_t stream, const char *who) {
+  if (const int r = gemm_split_ranks(M, N, K); r >= 2)
+    return launch_gemm_splitk<T>(M, N, K, r, epi, a, b, dt, stream, who);
   if (gemm_bn(M, N) == 256) return launch_gemm_t<T, 256>(M, N, K, epi, a, b, dt, stream, who);
   return launch_gemm_t<T, 128>(M, N, K, epi, a, b, dt, stream, who);
 }

@@ -47,16 +47,22 @@ struct GemmShape {
   int32_t tiles_m, tiles_n;
 };
 
-// ---- epilogues (called by each epilogue thread for its row of one output tile) -------------
+// ---- accumulator access (what the epilogues read) ------------------------------------------
 
-// Load 32 consecutive f32 accumulator columns of this thread's row.
-__device__ __forceinline__ void acc_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  tc::ld32(taddr, r);
-  tc::wait_ld();
+// This thread's row of the tile's f32 accumulator in TMEM. ld32 is a warp-collective tcgen05.ld:
+// every lane of the warp calls it with the same column.
+struct TmemAcc {
+  uint32_t taddr;  // TMEM address of (this warp's lane quadrant, column 0 of the tile)
+  __device__ __forceinline__ void ld32(int col, float (&v)[32]) const {
+    uint32_t r[32];
+    tc::ld32(taddr + col, r);
+    tc::wait_ld();
 #pragma unroll
-  for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
-}
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+  }
+};
+
+// ---- epilogues (called by each epilogue thread for its row of one output tile) -------------
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T x) {
@@ -86,8 +92,8 @@ struct QkvEpilogue {
   int32_t num_heads, num_kv_heads, head_dim, num_blocks, block_size, max_position;
 
   // One row (token) of a 128 x BN tile: BN / head_dim whole heads starting at column col0.
-  template <int BN>
-  __device__ void operator()(uint32_t tacc, int row, int col0, const GemmShape &s) const {
+  template <int BN, class Acc>
+  __device__ void operator()(const Acc &acc, int row, int col0, const GemmShape &s) const {
     const bool row_ok = row < s.M;
     const int half = head_dim / 2;
     int pos = 0, slot = -1;
@@ -101,7 +107,7 @@ struct QkvEpilogue {
       const int gh = f0 / head_dim;
       const bool is_q = gh < num_heads, is_k = !is_q && gh < num_heads + num_kv_heads;
       const T *nw = is_q ? q_norm : (is_k ? k_norm : nullptr);
-      const uint32_t ta = tacc + hl * head_dim;
+      const int ta = hl * head_dim;  // accumulator column of this head
       // Destination row, or null when this row writes nothing for this head.
       T *dst = nullptr;
       bool rope_ok = true;
@@ -131,7 +137,7 @@ struct QkvEpilogue {
         float ss = 0.f;
         for (int c = 0; c < head_dim / 32; ++c) {
           float v[32];
-          acc_ld32(ta + c * 32, v);
+          acc.ld32(ta + c * 32, v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float x = v[e] + (bias ? to_f32(bias[f0 + c * 32 + e]) : 0.f);
@@ -143,8 +149,8 @@ struct QkvEpilogue {
       // Rotate-half RoPE pairs column i with column i + head_dim/2 (i < head_dim/2).
       for (int c = 0; c < half / 32; ++c) {
         float a[32], b[32];
-        acc_ld32(ta + c * 32, a);
-        acc_ld32(ta + half + c * 32, b);
+        acc.ld32(ta + c * 32, a);
+        acc.ld32(ta + half + c * 32, b);
         if (dst == nullptr) continue;
         const int i0 = c * 32;
 #pragma unroll
@@ -186,14 +192,14 @@ struct ResidualEpilogue {
   T *out;                 // [M, N]
   const T *residual;      // [M, N] or null
 
-  template <int BN>
-  __device__ void operator()(uint32_t tacc, int row, int col0, const GemmShape &s) const {
+  template <int BN, class Acc>
+  __device__ void operator()(const Acc &acc, int row, int col0, const GemmShape &s) const {
     const bool row_ok = row < s.M;
     for (int c = 0; c < BN / 32; ++c) {
       const int col = col0 + c * 32;  // warp-uniform
       if (col >= s.N) break;
       float v[32];
-      acc_ld32(tacc + c * 32, v);
+      acc.ld32(c * 32, v);
       if (!row_ok) continue;
       const size_t base = size_t(row) * s.N + col;
       if (residual) {
@@ -313,7 +319,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc::fence_after();
       const int m = t / s.tiles_n, n = t % s.tiles_n;
-      epi.template operator()<BN>(tmem + lane_off + buf * BN, m * 128 + q * 32 + lane, n * BN, s);
+      epi.template operator()<BN>(TmemAcc{tmem + lane_off + buf * BN}, m * 128 + q * 32 + lane,
+                                  n * BN, s);
       tc::fence_before();
       mbar_arrive(bar(C::AEMPTY + buf));
     }
@@ -324,6 +331,219 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc::fence_after();
     tc::dealloc(tmem, C::kTmemCols);
   }
+}
+
+// ---- split-K over a thread-block cluster (small M) --------------------------------------------
+//
+// When the output has too few 128 x BN tiles to occupy the GPU (decode: 64 tokens), each tile is
+// computed by a cluster of S CTAs that split K. Each CTA accumulates its K slice in TMEM, copies
+// the f32 partial to its own shared memory, and signals every CTA of the cluster; CTA r then
+// sums rows [r*R, (r+1)*R) of all S partials through distributed shared memory and runs the
+// epilogue on them. No global workspace; the waits between CTAs are bounded mbarrier waits.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster; orders shared-memory accesses across the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (the arrivals come from other CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t phase) {
+  if (mbar_try_wait_cluster(bar, phase)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait_cluster(bar, phase)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+constexpr int kSplitMaxRanks = 8;
+
+// One row of the tile summed over the cluster's partials (f32 [128][BN + 4] in each CTA).
+struct SplitAcc {
+  uint32_t row_addr[kSplitMaxRanks];  // shared::cluster address of this row in each CTA
+  int nranks;
+  __device__ __forceinline__ void ld32(int col, float (&v)[32]) const {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = 0.f;
+    for (int p = 0; p < nranks; ++p) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float x0, x1, x2, x3;
+        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(x0), "=f"(x1), "=f"(x2), "=f"(x3)
+                     : "r"(row_addr[p] + uint32_t(col + 4 * q) * 4u)
+                     : "memory");
+        v[4 * q] += x0;
+        v[4 * q + 1] += x1;
+        v[4 * q + 2] += x2;
+        v[4 * q + 3] += x3;
+      }
+    }
+  }
+};
+
+template <typename T, int BN, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_splitk_kernel(const __grid_constant__ GemmShape s, const __grid_constant__ Epi epi,
+                          const __grid_constant__ CUtensorMap tm_a,
+                          const __grid_constant__ CUtensorMap tm_b) {
+  using C = GemmCfg<BN>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int kPitch = BN + 4;  // f32 row pitch of the partial (bank-conflict padding)
+  static_assert(128 * kPitch * 4 <= C::kBarOff, "partial must fit in the operand ring");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank(), nranks = cluster_nctarank();
+  const int tile = int(cluster_id_x());
+  const int m = tile / s.tiles_n, n = tile % s.tiles_n;
+  const int num_k = (s.K + kGemmBK - 1) / kGemmBK;
+  const int kb0 = int(int64_t(num_k) * rank / nranks), kb1 = int(int64_t(num_k) * (rank + 1) / nranks);
+  // Barriers: FULL/EMPTY ring, AFULL (partial ready in TMEM), and AEMPTY reused as "every CTA's
+  // partial is in its shared memory" (128 epilogue threads x nranks arrivals).
+  const int PREADY = C::AEMPTY;
+
+  if (tid == 0) {
+    for (int i = 0; i < C::NBARS; ++i) mbar_init(bar(i), i == PREADY ? 128 * int(nranks) : 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::alloc(smem_u32(s_tmem), C::kTmemCols);
+    tc::relinquish();
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  cluster_sync();  // every CTA's barriers are initialised before any remote arrive
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      bool ok = true;
+      for (int kb = kb0, it = 0; kb < kb1 && ok; ++kb, ++it) {
+        const int st = it % C::kStages;
+        if (it >= C::kStages && !(ok = mbar_wait(bar(C::EMPTY + st), ((it / C::kStages) - 1) & 1)))
+          break;
+        mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
+        const uint32_t a = sbase + st * C::kStageBytes;
+        tma_load_2d(a, &tm_a, bar(C::FULL + st), kb * kGemmBK, m * 128);
+        tma_load_2d(a + C::kABytes, &tm_b, bar(C::FULL + st), kb * kGemmBK, n * BN);
+      }
+      if (!ok) report(FA_DEVERR_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(kBf16, 128, BN, false, false);
+      bool ok = true;
+      for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
+        const int st = it % C::kStages;
+        if (!(ok = mbar_wait(bar(C::FULL + st), (it / C::kStages) & 1))) break;
+        tc::fence_after();
+        const uint32_t a = sbase + st * C::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < kGemmBK / 16; ++kk)
+          tc::mma_ss(tmem, tc::sw128_desc(a + kk * 32, 16, 1024),
+                     tc::sw128_desc(a + C::kABytes + kk * 32, 16, 1024), idesc,
+                     (kb > kb0 || kk > 0) ? 1u : 0u);
+        tc::commit(bar(C::EMPTY + st));
+      }
+      if (!ok) report(FA_DEVERR_TIMEOUT);
+      tc::commit(bar(C::AFULL));
+      tc::commit(bar(C::DRAIN));  // every MMA issued above has completed once this arrives
+      mbar_wait(bar(C::DRAIN), 0);
+    }
+  } else {
+    const int q = warp & 3;
+    const uint32_t lane_off = uint32_t(q * 32) << 16;
+    const int r = q * 32 + lane;  // tile row of this thread's TMEM lane
+    float *part = reinterpret_cast<float *>(smem);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(bar(C::AFULL), 0));
+    if (ok) {
+      tc::fence_after();
+      // This CTA's partial -> shared memory (the operand ring is idle: every MMA has completed).
+      const TmemAcc own{tmem + lane_off};
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        own.ld32(c * 32, v);
+        float4 *dst = reinterpret_cast<float4 *>(part + r * kPitch + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+      }
+    } else if (lane == 0) {
+      report(FA_DEVERR_TIMEOUT);
+    }
+    tc::fence_before();
+    // Tell every CTA of the cluster (this one included) that this thread's row is in place.
+    for (uint32_t p = 0; p < nranks; ++p) mbar_arrive_remote(map_to_rank(bar(PREADY), p));
+    ok = mbar_wait_cluster(bar(PREADY), 0) && ok;
+    if (!ok) {
+      report(FA_DEVERR_TIMEOUT);
+    } else {
+      // Rows [rank*R, rank*R + R) of the tile: summed over all partials, then the epilogue.
+      const int R = (128 + int(nranks) - 1) / int(nranks);
+      const int t = tid - 64;  // 0..127 over the four epilogue warps
+      const int row = int(rank) * R + t;
+      if (t < R && row < 128) {
+        SplitAcc acc;
+        acc.nranks = int(nranks);
+        const uint32_t own_row = smem_u32(part + row * kPitch);
+        for (uint32_t p = 0; p < nranks; ++p) acc.row_addr[p] = map_to_rank(own_row, p);
+        epi.template operator()<BN>(acc, m * 128 + row, n * BN, s);
+      }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::dealloc(tmem, C::kTmemCols);
+  }
+  cluster_sync();  // no CTA leaves while another may still read its partial
 }
 
 }  // namespace fa
