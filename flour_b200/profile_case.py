@@ -3,11 +3,15 @@
     python -m flour_b200.profile_case decode  [--launches 3] [--batch 64] [--seed 1000]
     python -m flour_b200.profile_case longctx [--launches 3]
     python -m flour_b200.profile_case prefill [--launches 3]
+    python -m flour_b200.profile_case qkv     [--launches 3] [--tokens 13490]
+    python -m flour_b200.profile_case oproj   [--launches 3] [--tokens 13490]
 
 `decode` is one layer of the C2 configuration (64 sequences, ctx ~ U[512, 4096], ~0.6 GB of
 KV: larger than L2, a few GB at most on the device). `longctx` is 4 sequences of the C4
 distribution (split-K heavy). `prefill` is one layer of C3. Each case runs one warm-up launch
-and then `--launches` launches of the kernel under test, and exits 0.
+and then `--launches` launches of the kernel under test, and exits 0. `qkv` / `oproj` are the
+fused Llama-3-8B projections (hidden 4096) at `--tokens` tokens (13490 = one C3 batch: the
+activations and weights exceed L2).
 """
 
 from __future__ import annotations
@@ -24,7 +28,8 @@ from .workloads import LLAMA8B, c2_contexts, c4_contexts, make_c3, make_decode
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "longctx", "prefill"])
+    ap.add_argument("case", choices=["decode", "longctx", "prefill", "qkv", "oproj"])
+    ap.add_argument("--tokens", type=int, default=13490)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--seed", type=int, default=1000)
@@ -41,6 +46,32 @@ def main() -> int:
                              scale, b.max_context_len, ws, out=out)
         torch.cuda.synchronize()
         print(f"{a.case}: {b.kv_bytes_per_layer() + b.io_bytes_per_layer()} algorithmic bytes/launch")
+    elif a.case in ("qkv", "oproj"):
+        from .paged import rope_tables
+        T, hidden, hq, hkv, d = a.tokens, 4096, 32, 8, 128
+        g = torch.Generator(device=dev).manual_seed(a.seed)
+        x = torch.randn(T, hidden, device=dev, generator=g).to(torch.bfloat16)
+        if a.case == "qkv":
+            n = (hq + 2 * hkv) * d
+            w = (torch.randn(n, hidden, device=dev, generator=g) / 64).to(torch.bfloat16)
+            kc = torch.zeros(T // 16 + 8, hkv, 16, d, device=dev, dtype=torch.bfloat16)
+            vc = torch.zeros_like(kc)
+            pos = torch.arange(T, dtype=torch.int32, device=dev) % 8192
+            slots = torch.arange(T, dtype=torch.int32, device=dev)
+            cos, sin = rope_tables(d, 8192, 500000.0, torch.bfloat16, dev)
+            q = torch.empty(T, hq, d, device=dev, dtype=torch.bfloat16)
+            for _ in range(1 + a.launches):
+                ops.qkv_rope_cache(x, w, kc, vc, pos, slots, hq, cos, sin, q_out=q)
+            flops = 2 * T * hidden * n
+        else:
+            w = (torch.randn(hidden, hq * d, device=dev, generator=g) / 64).to(torch.bfloat16)
+            attn = torch.randn(T, hq * d, device=dev, generator=g).to(torch.bfloat16)
+            out = torch.empty(T, hidden, device=dev, dtype=torch.bfloat16)
+            for _ in range(1 + a.launches):
+                ops.o_proj_residual(attn, w, x, out=out)
+            flops = 2 * T * hq * d * hidden
+        torch.cuda.synchronize()
+        print(f"{a.case}: {flops} algorithmic FLOPs/launch")
     else:
         b = make_c3(dev, seed=a.seed)
         ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
