@@ -73,19 +73,6 @@ __device__ __forceinline__ void st_global_v8(void *ptr, const uint32_t *r) {
                : "memory");
 }
 
-// 2^x for two packed 16-bit values (one SFU instruction for the pair). The inputs are rounded to
-// the 16-bit type first, so this suits values that end up in that type anyway.
-template <typename T> __device__ __forceinline__ uint32_t ex2_x2(uint32_t x);
-template <> __device__ __forceinline__ uint32_t ex2_x2<__nv_bfloat16>(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-template <> __device__ __forceinline__ uint32_t ex2_x2<__half>(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
 // The two values of a packed 16-bit pair as floats (lo, hi).
 template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t v);
 template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {

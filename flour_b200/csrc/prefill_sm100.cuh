@@ -68,14 +68,6 @@ constexpr int kPfPages = kPfBN / kPage;     // 8 pages per KV tile
 constexpr int kPfStages = 2;
 constexpr float kPfRescale = 8.0f;          // lazy-rescale threshold (log2 units)
 constexpr int kPfMaxSeqs = 2048;            // sequences per launch (chunk table in smem)
-#ifndef FA_PF_EXP_PACKED
-#define FA_PF_EXP_PACKED 0                  // 1: exponentials as packed 16-bit pairs
-#endif
-constexpr bool kPfExpPacked = FA_PF_EXP_PACKED != 0;
-#ifndef FA_PF_TRUNC_P
-#define FA_PF_TRUNC_P 1                     // bf16 P by truncation (ALU) instead of cvt (SFU)
-#endif
-constexpr bool kPfTruncP = FA_PF_TRUNC_P != 0;
 
 struct PfItem {
   int32_t kind;  // 0 work, 1 invalid sequence data (rows are zeroed), 2 no more work
