@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--no-projections", action="store_true")
     ap.add_argument("--no-c5", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the head-sharded decode (N > 1)")
     return ap.parse_args()
 
 
@@ -344,6 +345,12 @@ def run_ours(args):
         longctx = run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks,
                               barrier, world)
 
+    # ---- head-sharded decode with the all-gather fused into the kernel (N > 1) -----------------
+    tp = None
+    if world > 1 and not args.no_tp:
+        tp = run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier)
+        torch.cuda.empty_cache()
+
     # ---- the fused projections either side of attention ---------------------------------------
     proj = None
     if not args.no_projections:
@@ -395,6 +402,8 @@ def run_ours(args):
             line["projections"] = proj
         if c5:
             line["c5"] = c5
+        if tp:
+            line["tp_decode"] = tp
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
@@ -651,6 +660,91 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
            "prefill_tokens": int(pf_len[is_pf].sum()),
            "decode_kv_gb_per_step": round(dec_bytes / 1e9, 3),
            "prefill_tflop_per_step": round(pf_flops / 1e12, 3)}
+    return res
+
+
+def run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
+    """Head-sharded decode of ONE C2 batch (64 sequences, 32 layers) over all ranks: rank r holds
+    KV heads [8r/N, 8(r+1)/N) of every layer's pool and the matching query heads (strong
+    scaling). Fused: fa_paged_decode_tp stores each rank's head outputs into every rank's output
+    buffer over NVLink, then fa_tp_wait; NCCL: fa_paged_decode into a local buffer followed by
+    all_gather_into_tensor. Both steps are CUDA graphs of the 32 layers; after either one every
+    rank holds the full [64, 32, 128] output of every layer."""
+    import torch.distributed as dist
+    from flour_b200.tp import HeadShardedGroup, head_shard, torch_exchange
+    from flour_b200.workloads import LLAMA8B, Heads, c2_contexts, make_decode
+    h = LLAMA8B
+    if h.num_kv_heads % world:
+        return None
+    kv0, kv1, h0, h1 = head_shard(h.num_heads, h.num_kv_heads, world, rank)
+    hs = Heads(h1 - h0, kv1 - kv0, h.head_dim)
+    # Same sequences, contexts and block tables on every rank (same seed); this rank's heads.
+    b = make_decode(hs, c2_contexts(args.seed), torch.bfloat16, dev, args.seed, num_layers=NUM_LAYERS)
+    B = b.num_seqs
+    scale = 1.0 / math.sqrt(h.head_dim)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 7 + rank)
+    qs = [torch.randn((B, hs.num_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
+          for _ in range(NUM_LAYERS)]
+    ws = ops.Workspace(dev)
+    ws.get(ops.workspace_size(B, hs.num_heads, hs.num_kv_heads, h.head_dim, b.max_context_len, 1))
+    grp = HeadShardedGroup(world, rank, B, h.num_heads, h.head_dim, torch.bfloat16,
+                           torch_exchange(), dev)
+    loc = [torch.empty_like(q) for q in qs]
+    gathered = [torch.empty((world,) + tuple(q.shape), dtype=q.dtype, device=dev) for q in qs]
+
+    def step_fused():
+        for l in range(NUM_LAYERS):
+            grp.decode(qs[l], b.k_caches[l], b.v_caches[l], b.block_tables, b.context_lens,
+                       hs.n_rep, scale, b.max_context_len, ws)
+
+    def step_nccl():
+        for l in range(NUM_LAYERS):
+            ops.paged_decode(qs[l], b.k_caches[l], b.v_caches[l], b.block_tables, b.context_lens,
+                             hs.n_rep, scale, b.max_context_len, ws, out=loc[l])
+            dist.all_gather_into_tensor(gathered[l], loc[l])
+
+    res = {"config": "C2 batch (64 seqs, 32 layers, Llama-3-8B heads) head-sharded over the ranks",
+           "scaling": "strong", "tp": world,
+           "kv_gb_per_step": round(float(b.ctx_host.sum()) * h.num_kv_heads * h.head_dim * 4
+                                   * NUM_LAYERS / 1e9, 3)}
+    graphs = {}
+    try:
+        for name, fn in (("fused", step_fused), ("nccl", step_nccl)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            graphs[name] = graph
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            barrier()
+            reps = max(20, args.steps // 4)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+            res[f"{name}_ms_per_step"] = round(ms, 4)
+            res[f"{name}_gbps"] = round(res["kv_gb_per_step"] / (ms / 1e3), 1)
+        status = ops.device_status()
+        assert status == 0, f"head-sharded decode reported device status 0x{status:x}"
+        # The fused output of the last layer equals the NCCL-gathered one (same kernel per head).
+        full = grp.output(grp.epoch, B)
+        ref = gathered[-1].permute(1, 0, 2, 3).reshape(B, h.num_heads, h.head_dim)
+        res["fused_equals_nccl"] = bool(torch.equal(full, ref))
+        res["speedup_vs_nccl"] = round(res["nccl_ms_per_step"] / res["fused_ms_per_step"], 3)
+    finally:
+        graphs.clear()  # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize()
+        barrier()
+        grp.close()
     return res
 
 

@@ -64,6 +64,31 @@ class FaQkvWeights(ctypes.Structure):
 
 _WP = ctypes.POINTER(FaQkvWeights)
 
+FA_MAX_TP = 8
+
+
+class FaIpcHandle(ctypes.Structure):
+    """``fa_ipc_handle``: a CUDA IPC memory handle, 64 opaque bytes."""
+
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+class FaTpGroup(ctypes.Structure):
+    """``fa_tp_group``: the ranks' output buffers and flag arrays as mapped in this process."""
+
+    _fields_ = [
+        ("tp", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("out", ctypes.c_void_p * FA_MAX_TP),
+        ("flags", ctypes.c_void_p * FA_MAX_TP),
+        ("done_counter", ctypes.c_void_p),
+        ("epoch_counter", ctypes.c_void_p),
+    ]
+
+
+_HP = ctypes.POINTER(FaIpcHandle)
+_GP = ctypes.POINTER(FaTpGroup)
+
 SIGNATURES = {
     "fa_abi_version": (_I32, []),
     "fa_status_string": (ctypes.c_char_p, [_I32]),
@@ -82,6 +107,13 @@ SIGNATURES = {
                                 _F, _P, _SZ, _P]),
     "fa_qkv_rope_cache": (_I32, [_LP, _WP, _P, _P, _P, _I32, _P, _P]),
     "fa_o_proj_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P]),
+    "fa_ipc_alloc": (_I32, [_SZ, ctypes.POINTER(_P), _HP]),
+    "fa_ipc_free": (_I32, [_P]),
+    "fa_ipc_open": (_I32, [_HP, ctypes.POINTER(_P)]),
+    "fa_ipc_close": (_I32, [_P]),
+    "fa_paged_decode_tp": (_I32, [_GP, _LP, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F,
+                                  ctypes.c_uint32, _P, _SZ, _P]),
+    "fa_tp_wait": (_I32, [_GP, ctypes.c_uint32, _I64, _P]),
 }
 
 

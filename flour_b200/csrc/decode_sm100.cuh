@@ -26,15 +26,34 @@
 // Split-K merge. Splits write (O/l, log2-sum-exp) partials to the workspace; the last CTA of a
 // (sequence, kv_head) to finish (atomic ticket, no waiting) merges them and resets the ticket.
 // Sequences with a single split write the output directly.
+//
+// Head-sharded groups (tensor parallel over KV heads, one GPU per rank). The final write of each
+// (sequence, kv head) goes to every rank's output buffer (peer memory over NVLink, mapped by
+// CUDA IPC) at the rank's head offset, so the all-gather of the per-head outputs happens inside
+// the kernel. After its writes, each (sequence, kv head) bumps a done counter (system-scope fence
+// first); the last one publishes `epoch` into every rank's flag slot for this rank with a
+// system-scope release store. Consumers wait for all ranks' flags (fa_tp_wait).
 #pragma once
 
 #include "fa_common.cuh"
 
 namespace fa {
 
+constexpr int kMaxTp = 8;  // ranks of a head-sharded group
+
 struct DecodeParams {
   const void *q;                 // [num_seqs, num_heads, HD]
-  void *out;                     // [num_seqs, num_heads, HD]
+  void *out;                     // [num_seqs, num_heads, HD] (single-GPU mode)
+  // Head-sharded mode (n_outs > 0): outs[r] = rank r's [num_seqs, out_heads, HD] buffer; this
+  // rank's heads start at out_head0. Otherwise out / num_heads / head 0.
+  void *outs[kMaxTp];
+  uint32_t *flag_slots[kMaxTp];  // &flags_of_rank_r[this rank]
+  int32_t *done_counter;         // back to 0 after every launch
+  uint32_t *epoch_counter;       // device epoch, advanced by the launch when epoch == 0
+  int32_t n_outs;
+  int32_t out_heads;
+  int32_t out_head0;
+  uint32_t epoch;
   const int32_t *context_lens;   // [num_seqs]
   const int32_t *block_tables;   // [num_seqs, max_blocks_per_seq]
   float *part_o;                 // [num_seqs, num_heads, max_splits, HD]
@@ -75,6 +94,48 @@ struct DecodeSmem {
                 "reduction scratch must fit in the ring");
 };
 
+// Store one output element of query head (b, hq) (hq counted within this launch's heads) to the
+// output buffer, or to every rank's buffer of a head-sharded group.
+template <typename T>
+__device__ __forceinline__ void store_out(const DecodeParams &p, int b, int hq, int HD, int x,
+                                          float v) {
+  const T e = Elem<T>::from_f(v);
+  if (p.n_outs == 0) {
+    static_cast<T *>(p.out)[(size_t(b) * p.num_heads + hq) * HD + x] = e;
+    return;
+  }
+  const size_t off = (size_t(b) * p.out_heads + p.out_head0 + hq) * HD + x;
+  for (int r = 0; r < p.n_outs; ++r) static_cast<T *>(p.outs[r])[off] = e;
+}
+
+// Publish epoch e into every rank's flag slot for this rank (after a system-scope fence).
+__device__ __forceinline__ void publish_epoch(uint32_t *const *slots, int n, uint32_t e) {
+  __threadfence_system();
+  for (int r = 0; r < n; ++r)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slots[r]), "r"(e) : "memory");
+}
+
+// The epoch a launch publishes: the host's, or (epoch 0) the next device epoch. Called by the
+// single thread that publishes; launches on one stream run one after the other.
+__device__ __forceinline__ uint32_t next_epoch(uint32_t host_epoch, uint32_t *counter) {
+  if (host_epoch != 0) return host_epoch;
+  const uint32_t e = *counter + 1;
+  *counter = e;
+  return e;
+}
+
+// Called by one thread after this CTA wrote the final output of one (sequence, kv head). In a
+// head-sharded group, the last of them publishes the epoch to every rank.
+__device__ __forceinline__ void output_done(const DecodeParams &p) {
+  if (p.n_outs == 0 || p.done_counter == nullptr) return;
+  __threadfence_system();  // this CTA's peer stores before the count
+  const int total = p.num_seqs * p.num_kv_heads;
+  if (atomicAdd(p.done_counter, 1) == total - 1) {
+    *p.done_counter = 0;   // ready for the next launch (stream order separates launches)
+    publish_epoch(p.flag_slots, p.n_outs, next_epoch(p.epoch, p.epoch_counter));
+  }
+}
+
 template <typename T, int HD, int NSTAGE>
 __global__ void __launch_bounds__(kDecodeThreads, 2)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
@@ -100,8 +161,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     // Nothing valid to attend to: zero this CTA's heads once (split 0) and report.
     if (split == 0) {
       if (tid == 0) report(FA_DEVERR_CONTEXT);
-      T *o = static_cast<T *>(p.out) + (size_t(b) * p.num_heads + size_t(kvh) * n_rep) * HD;
-      for (int x = tid; x < n_rep * HD; x += kDecodeThreads) o[x] = Elem<T>::from_f(0.f);
+      for (int x = tid; x < n_rep * HD; x += kDecodeThreads)
+        store_out<T>(p, b, kvh * n_rep + x / HD, HD, x % HD, 0.f);
+      __syncthreads();
+      if (tid == 0) output_done(p);
     }
     return;
   }
@@ -288,14 +351,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     }
     const size_t ob = size_t(b) * p.num_heads + hq0 + h;
     if (single) {
-      static_cast<T *>(p.out)[ob * HD + x] = Elem<T>::from_f(O / Lsum);
+      store_out<T>(p, b, hq0 + h, HD, x, O / Lsum);
     } else {
       const size_t pi = ob * p.max_splits + split;
       p.part_o[pi * HD + x] = O / Lsum;
       if (x == 0) p.part_lse[pi] = M + __log2f(Lsum);
     }
   }
-  if (single) return;
+  if (single) {
+    if (p.n_outs) {  // uniform: the whole CTA takes it or not
+      __syncthreads();
+      if (tid == 0) output_done(p);
+    }
+    return;
+  }
 
   // ---- last split of this (sequence, kv_head) merges the partials ------------------------
   __threadfence();
@@ -326,9 +395,45 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       O += w * __ldcg(po + size_t(sp) * HD);
       W += w;
     }
-    static_cast<T *>(p.out)[ob * HD + x] = Elem<T>::from_f(O / W);
+    store_out<T>(p, b, hq0 + h, HD, x, O / W);
   }
-  if (tid == 0) p.counters[b * p.num_kv_heads + kvh] = 0;  // ready for the next launch
+  if (p.n_outs) __syncthreads();  // uniform
+  if (tid == 0) {
+    p.counters[b * p.num_kv_heads + kvh] = 0;  // ready for the next launch
+    output_done(p);
+  }
+}
+
+// Head-sharded groups, empty batch: publish `epoch` to every rank without a decode launch.
+struct TpFlagSlots {
+  uint32_t *slot[kMaxTp];
+};
+__global__ void tp_publish_kernel(TpFlagSlots slots, int tp, uint32_t epoch, uint32_t *counter) {
+  if (threadIdx.x == 0) publish_epoch(slots.slot, tp, next_epoch(epoch, counter));
+}
+
+// Head-sharded groups: one thread per rank polls flags[s] (stored by rank s over NVLink) until
+// it reaches `epoch` (wrap-around order; 0 = this rank's device epoch). Bounded by device time
+// and by an iteration cap; on expiry it reports FA_DEVERR_TIMEOUT and returns.
+__global__ void tp_wait_kernel(const uint32_t *flags, int tp, uint32_t epoch,
+                               const uint32_t *counter, unsigned long long timeout_ns) {
+  const int s = threadIdx.x;
+  if (s >= tp) return;
+  if (epoch == 0) epoch = *counter;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  const unsigned long long max_iters = timeout_ns / 64 + 4096;  // sleeps are >= ~100 ns
+  for (unsigned long long it = 0;; ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+    if (int32_t(v - epoch) >= 0) return;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > timeout_ns || it >= max_iters) {
+      report(FA_DEVERR_TIMEOUT);
+      return;
+    }
+    __nanosleep(128);
+  }
 }
 
 }  // namespace fa

@@ -176,10 +176,16 @@ fa_status launch_decode_t(const fa::DecodeParams &p, const CUtensorMap &tk, cons
 
 constexpr int kDecodeStages = 3;
 
+// Head-sharded output targets of one decode call (NULL: plain single-GPU output).
+struct TpTargets {
+  const fa_tp_group *group;
+  uint32_t epoch;
+};
+
 fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const int32_t *ctx,
                         const int32_t *tables, int max_blocks, int num_seqs, int num_heads,
                         int n_rep, int max_context_len, float scale, void *ws, size_t ws_bytes,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const TpTargets *tpt = nullptr) {
   DecodePlan plan;
   if (!plan_decode(num_seqs, L->num_kv_heads, max_context_len, &plan))
     return fail(FA_EUNSUPPORTED, "decode: context of %d tokens needs more than %d splits",
@@ -211,6 +217,19 @@ fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const in
   p.max_splits = plan.max_splits;
   p.max_context_len = max_context_len;
   p.scale_log2 = scale * 1.4426950408889634f;
+  if (tpt) {
+    const fa_tp_group *g = tpt->group;
+    p.n_outs = g->tp;
+    p.out_heads = g->tp * num_heads;
+    p.out_head0 = g->rank * num_heads;
+    p.epoch = tpt->epoch;
+    p.done_counter = g->done_counter;
+    p.epoch_counter = g->epoch_counter;
+    for (int r = 0; r < g->tp; ++r) {
+      p.outs[r] = g->out[r];
+      p.flag_slots[r] = g->flags[r] + g->rank;
+    }
+  }
   const int64_t rows = int64_t(L->num_blocks) * L->num_kv_heads * L->block_size;
   CUtensorMap tk, tv;
   if (fa_status s = make_page_map(&tk, L->k_cache, rows, L->head_dim, L->dtype); s != FA_OK) return s;
@@ -837,6 +856,116 @@ fa_status fa_o_proj_residual(const void *attn, const void *weight, const void *r
   }
   fa::ResidualEpilogue<__half> epi{static_cast<__half *>(out), static_cast<const __half *>(residual)};
   return launch_gemm<__half>(num_tokens, out_features, in_features, epi, attn, weight, dtype, st, who);
+}
+
+// ---- head-sharded decode ------------------------------------------------------------------
+
+static_assert(FA_MAX_TP == fa::kMaxTp, "FA_MAX_TP and the kernel's rank limit differ");
+static_assert(sizeof(fa_ipc_handle) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+
+fa_status fa_ipc_alloc(size_t bytes, void **ptr_out, fa_ipc_handle *handle_out) {
+  if (!ptr_out || !handle_out) return fail(FA_EINVAL, "ipc_alloc: NULL output");
+  *ptr_out = nullptr;
+  if (bytes == 0) return fail(FA_EINVAL, "ipc_alloc: zero bytes");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "ipc_alloc: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(FA_ECUDA, "ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(handle_out->bytes, &h, sizeof(h));
+  *ptr_out = p;
+  return ok();
+}
+
+fa_status fa_ipc_free(void *ptr) {
+  if (!ptr) return ok();
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "ipc_free: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+fa_status fa_ipc_open(const fa_ipc_handle *handle, void **ptr_out) {
+  if (!handle || !ptr_out) return fail(FA_EINVAL, "ipc_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "ipc_open: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+fa_status fa_ipc_close(void *ptr) {
+  if (!ptr) return ok();
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "ipc_close: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+static fa_status check_tp_group(const fa_tp_group *g, const char *who) {
+  if (!g) return fail(FA_EINVAL, "%s: group is NULL", who);
+  if (g->tp < 1 || g->tp > FA_MAX_TP)
+    return fail(FA_EINVAL, "%s: tp %d outside [1, %d]", who, g->tp, FA_MAX_TP);
+  if (g->rank < 0 || g->rank >= g->tp)
+    return fail(FA_EINVAL, "%s: rank %d outside [0, %d)", who, g->rank, g->tp);
+  for (int r = 0; r < g->tp; ++r) {
+    if (!g->flags[r] || !aligned(g->flags[r], 4))
+      return fail(FA_EINVAL, "%s: flags[%d] is NULL or misaligned", who, r);
+  }
+  return FA_OK;
+}
+
+fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer, const void *query,
+                             const int32_t *context_lens, const int32_t *block_tables,
+                             int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
+                             int32_t n_rep, int32_t max_context_len, float scale, uint32_t epoch,
+                             void *workspace, size_t workspace_bytes, fa_stream_t stream) {
+  const char *who = "paged_decode_tp";
+  if (fa_status s = check_tp_group(group, who); s != FA_OK) return s;
+  if (epoch == 0 && !group->epoch_counter)
+    return fail(FA_EINVAL, "%s: epoch 0 (device epochs) needs group->epoch_counter", who);
+  for (int r = 0; r < group->tp; ++r)
+    if (!group->out[r] || !aligned(group->out[r], 16))
+      return fail(FA_EINVAL, "%s: out[%d] is NULL or not 16-byte aligned", who, r);
+  if (!group->done_counter) return fail(FA_EINVAL, "%s: done_counter is NULL", who);
+  if (fa_status s = check_attention_args(who, layer, query, group->out[group->rank], context_lens,
+                                         block_tables, max_blocks_per_seq, num_seqs, num_heads,
+                                         n_rep, max_context_len, scale);
+      s != FA_OK)
+    return s;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (num_seqs == 0) {  // nothing to write; the peers still wait for this epoch
+    fa::TpFlagSlots slots{};
+    for (int r = 0; r < group->tp; ++r) slots.slot[r] = group->flags[r] + group->rank;
+    fa::tp_publish_kernel<<<1, 32, 0, st>>>(slots, group->tp, epoch, group->epoch_counter);
+    return check_launch(who);
+  }
+  if (max_context_len < 1) return fail(FA_ERANGE, "%s: max_context_len must be >= 1", who);
+  if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "%s: more than 65535 sequences per call", who);
+  if (!decode_fast_path(layer, n_rep, query, group->out[group->rank]))
+    return fail(FA_EUNSUPPORTED,
+                "%s: needs a 16-bit pool, block_size 16, head_dim 64/128, n_rep <= 8 and "
+                "16-byte aligned buffers", who);
+  const TpTargets tpt{group, epoch};
+  return launch_decode(layer, query, nullptr, context_lens, block_tables, max_blocks_per_seq,
+                       num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                       workspace_bytes, st, &tpt);
+}
+
+fa_status fa_tp_wait(const fa_tp_group *group, uint32_t epoch, int64_t timeout_ns, fa_stream_t stream) {
+  const char *who = "tp_wait";
+  if (fa_status s = check_tp_group(group, who); s != FA_OK) return s;
+  if (epoch == 0 && !group->epoch_counter)
+    return fail(FA_EINVAL, "%s: epoch 0 (device epochs) needs group->epoch_counter", who);
+  if (timeout_ns < 1000 || timeout_ns > 10000000000LL)
+    return fail(FA_ERANGE, "%s: timeout_ns %lld outside [1e3, 1e10]", who, (long long)timeout_ns);
+  fa::tp_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      group->flags[group->rank], group->tp, epoch, group->epoch_counter,
+      (unsigned long long)timeout_ns);
+  return check_launch(who);
 }
 
 }  // extern "C"

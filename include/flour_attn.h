@@ -13,7 +13,7 @@
  *
  * Conventions
  *   - Device memory (pools, queries, outputs, tables, workspace) is owned by the caller. No
- *     entry point allocates device memory.
+ *     entry point allocates device memory except fa_ipc_alloc (head-sharded group buffers).
  *   - Every call is ordered on `stream` and returns before the GPU work finishes.
  *   - Host-side argument checks return FA_EINVAL / FA_ERANGE / FA_EUNSUPPORTED without
  *     launching anything; fa_last_error_message() then describes the rejection (thread-local).
@@ -69,7 +69,7 @@ typedef enum fa_dtype { FA_F32 = 0, FA_BF16 = 1, FA_F16 = 2 } fa_dtype;
 #define FA_DEVERR_BLOCK_ID 0x1   /* block table entry outside [0, num_blocks) */
 #define FA_DEVERR_CONTEXT 0x2    /* context_len < q_len, or > max_blocks_per_seq*block_size */
 #define FA_DEVERR_SLOT 0x4       /* slot_mapping entry outside [-1, num_blocks*block_size) */
-#define FA_DEVERR_TIMEOUT 0x8    /* a bounded wait on an mbarrier gave up */
+#define FA_DEVERR_TIMEOUT 0x8    /* a bounded wait (mbarrier, head-sharded flags) gave up */
 #define FA_DEVERR_SEQLEN 0x10    /* cu_seqlens_q not non-decreasing or past total_q */
 #define FA_DEVERR_PAIR 0x20      /* copy_blocks pair entry outside [0, num_blocks) */
 #define FA_DEVERR_POSITION 0x40  /* RoPE position outside [0, max_position) */
@@ -243,6 +243,69 @@ FA_API fa_status fa_qkv_rope_cache(const fa_kv_layer *layer, const fa_qkv_weight
 FA_API fa_status fa_o_proj_residual(const void *attn, const void *weight, const void *residual,
                                     void *out, int32_t num_tokens, int32_t in_features,
                                     int32_t out_features, int32_t dtype, fa_stream_t stream);
+
+/* ---- head-sharded decode (tensor parallel over KV heads, one process per GPU) ----------
+ * The reference runs attention on one CPU and has no sharding (its plan shards sequences,
+ * which needs no exchange). This optional mode splits a layer's KV heads over `tp` GPUs: rank r
+ * holds KV heads [r*kv/tp, (r+1)*kv/tp) of every block and the matching query heads. The decode
+ * kernel writes each finished (sequence, kv head) output into EVERY rank's output buffer at the
+ * rank's head offset (stores into peer memory over NVLink, mapped with CUDA IPC), so the
+ * all-gather of the head outputs is part of the attention kernel, with no separate collective.
+ * The kernel's last CTA then stores `epoch` into slot [rank] of every rank's flag array
+ * (system-scope release); fa_tp_wait makes a stream wait (bounded) until all ranks published
+ * the epoch into this rank's flags.
+ *
+ * Buffers: every rank allocates its output buffers, a flag array of FA_MAX_TP u32 and a done
+ * counter with fa_ipc_alloc (zero-filled), exchanges the handles, and opens its peers'
+ * handles with fa_ipc_open. Epochs start at 1 and grow by one per call. A rank may publish
+ * epoch e+1 into a peer before that peer waited for epoch e, so the group alternates two
+ * output buffers by epoch parity: the buffer of epoch e is rewritten at epoch e+2, which every
+ * rank starts only after fa_tp_wait(e+1), i.e. after each peer enqueued its uses of epoch e's
+ * output ahead of its decode of epoch e+1 on the same stream. */
+#define FA_MAX_TP 8
+typedef struct fa_ipc_handle {
+  unsigned char bytes[64]; /* cudaIpcMemHandle_t */
+} fa_ipc_handle;
+
+/* cudaMalloc + zero fill + cudaIpcGetMemHandle on the current device. */
+FA_API fa_status fa_ipc_alloc(size_t bytes, void **ptr_out, fa_ipc_handle *handle_out);
+FA_API fa_status fa_ipc_free(void *ptr);
+/* Map a peer process's allocation into this process (peer access enabled lazily). */
+FA_API fa_status fa_ipc_open(const fa_ipc_handle *handle, void **ptr_out);
+FA_API fa_status fa_ipc_close(void *ptr);
+
+typedef struct fa_tp_group {
+  int32_t tp;                  /* ranks, 1..FA_MAX_TP */
+  int32_t rank;                /* this process's rank */
+  void *out[FA_MAX_TP];        /* rank r's output buffer [num_seqs, tp*num_heads, head_dim] for
+                                  this call, as mapped in this process; 16-byte aligned */
+  uint32_t *flags[FA_MAX_TP];  /* rank r's flag array (FA_MAX_TP u32), as mapped here */
+  int32_t *done_counter;       /* this rank's own counter (4 bytes, zero, device memory) */
+  uint32_t *epoch_counter;     /* this rank's device epoch (4 bytes, zero): used when epoch == 0 */
+} fa_tp_group;
+
+/* fa_paged_decode over this rank's head shard (layer = the rank's KV heads, query [num_seqs,
+ * num_heads, head_dim] = its query heads), writing the rows into every rank's group->out at
+ * head offset rank*num_heads, then publishing the epoch. Requires the fast decode path (16-bit
+ * pool, block_size 16, head_dim 64/128, n_rep <= 8). Does not wait.
+ * epoch >= 1: publish that value (the host counts epochs).
+ * epoch == 0: the kernel adds one to *group->epoch_counter and publishes the result, so the
+ *   calls can be captured in a CUDA graph and replayed (every rank must make the same calls;
+ *   a captured sequence should hold an even number of calls so that the output buffers keep
+ *   alternating across replays). Use one of the two modes per group. */
+FA_API fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer,
+                                    const void *query, const int32_t *context_lens,
+                                    const int32_t *block_tables, int32_t max_blocks_per_seq,
+                                    int32_t num_seqs, int32_t num_heads, int32_t n_rep,
+                                    int32_t max_context_len, float scale, uint32_t epoch,
+                                    void *workspace, size_t workspace_bytes, fa_stream_t stream);
+
+/* Make `stream` wait until every rank published `epoch` (or a later one) into this rank's
+ * flags; epoch 0 means this rank's current device epoch (*group->epoch_counter, read when the
+ * wait starts). The wait gives up after timeout_ns (1 us .. 10 s) of device time, sets
+ * FA_DEVERR_TIMEOUT (fa_device_status) and returns, leaving the context usable. */
+FA_API fa_status fa_tp_wait(const fa_tp_group *group, uint32_t epoch, int64_t timeout_ns,
+                            fa_stream_t stream);
 
 #ifdef __cplusplus
 }
