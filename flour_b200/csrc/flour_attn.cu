@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "attn_generic.cuh"
 #include "cache_ops.cuh"
@@ -176,6 +177,30 @@ fa_status launch_decode_t(const fa::DecodeParams &p, const CUtensorMap &tk, cons
 
 constexpr int kDecodeStages = 3;
 
+// Split-K merge tickets must be zero when a decode launch starts. Every launch returns its own
+// tickets to zero, but a caller workspace reused with another shape may hold split-K partials
+// where the new tickets go. Per workspace base pointer, remember the smallest ticket region of
+// any launch so far: the bytes below it are zero after every launch (and after every CUDA-graph
+// replay of a captured one); a launch whose tickets reach past it zeroes the difference first.
+std::mutex g_ticket_mu;
+std::unordered_map<uintptr_t, size_t> g_ticket_clean;
+
+fa_status zero_stale_tickets(void *ws, size_t ticket_bytes, cudaStream_t stream) {
+  size_t clean;
+  {
+    std::lock_guard<std::mutex> lock(g_ticket_mu);
+    const auto [it, fresh] = g_ticket_clean.try_emplace(reinterpret_cast<uintptr_t>(ws), ticket_bytes);
+    if (fresh) return FA_OK;  // a workspace is zero-filled before its first use
+    clean = it->second;
+    if (ticket_bytes < clean) it->second = ticket_bytes;
+  }
+  if (ticket_bytes <= clean) return FA_OK;
+  const cudaError_t e =
+      cudaMemsetAsync(static_cast<char *>(ws) + clean, 0, ticket_bytes - clean, stream);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "decode: zeroing merge tickets: %s", cudaGetErrorString(e));
+  return FA_OK;
+}
+
 // Head-sharded output targets of one decode call (NULL: plain single-GPU output).
 struct TpTargets {
   const fa_tp_group *group;
@@ -185,7 +210,8 @@ struct TpTargets {
 fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const int32_t *ctx,
                         const int32_t *tables, int max_blocks, int num_seqs, int num_heads,
                         int n_rep, int max_context_len, float scale, void *ws, size_t ws_bytes,
-                        cudaStream_t stream, const TpTargets *tpt = nullptr) {
+                        cudaStream_t stream, const TpTargets *tpt = nullptr,
+                        bool caller_workspace = true) {
   DecodePlan plan;
   if (!plan_decode(num_seqs, L->num_kv_heads, max_context_len, &plan))
     return fail(FA_EUNSUPPORTED, "decode: context of %d tokens needs more than %d splits",
@@ -197,6 +223,8 @@ fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const in
     if (ws_bytes < w.bytes)
       return fail(FA_ERANGE, "decode: workspace of %zu bytes, %zu needed", ws_bytes, w.bytes);
     if (!aligned(ws, 256)) return fail(FA_EINVAL, "decode: workspace must be 256-byte aligned");
+    if (caller_workspace)
+      if (fa_status s = zero_stale_tickets(ws, w.lse_off, stream); s != FA_OK) return s;
   }
   fa::DecodeParams p{};
   p.q = q;
@@ -794,7 +822,7 @@ fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, v
   }
   return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq, num_seqs,
                        num_heads, n_rep, max_context_len, scale, scratch,
-                       FA_NOALLOC_DECODE_SCRATCH_BYTES, stream);
+                       FA_NOALLOC_DECODE_SCRATCH_BYTES, stream, nullptr, false);
 }
 
 fa_status fa_qkv_rope_cache(const fa_kv_layer *layer, const fa_qkv_weights *w, const void *x,

@@ -138,8 +138,10 @@ FA_API fa_status fa_read_block(const fa_kv_layer *layer, int32_t block_id, void 
 
 /* Bytes of workspace the attention entry points need for these sizes (split-K partials and
  * merge counters). 0 means no workspace is needed. The workspace must be zero-filled once
- * before its first use; the kernels leave the counters at zero when they finish. Calls that
- * run concurrently on different streams need separate workspaces. */
+ * before its first use; the kernels leave the counters at zero when they finish. One workspace
+ * may serve calls of different sizes (the library zeroes counters that land on an earlier
+ * call's partials) when it is always passed by the same base pointer. Calls that run
+ * concurrently on different streams need separate workspaces. */
 FA_API size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads,
                                          int32_t num_kv_heads, int32_t head_dim,
                                          int32_t max_context_len, int32_t max_seqlen_q);

@@ -111,6 +111,33 @@ def test_split_count_does_not_change_result_and_repeats_are_identical(device):
     check(b, o3, TOL_BF16)
 
 
+def test_workspace_reused_across_shapes(device):
+    # A few long sequences leave split-K partials right after their small ticket region; a
+    # larger batch then puts its tickets there. Results must equal runs on fresh workspaces,
+    # eagerly and when the small call is replayed from a CUDA graph in between.
+    small = make_decode(LLAMA8B, np.array([9000, 7000, 8000, 6000]), torch.bfloat16, device, 14)
+    big = make_decode(LLAMA8B, c2_contexts(15, batch=64), torch.bfloat16, device, 15)
+    want_small = run_decode(small, ops.Workspace(device)).clone()
+    want_big = run_decode(big, ops.Workspace(device)).clone()
+    ws = ops.Workspace(device)
+    ws.get(64 << 20)  # one buffer for every call below
+    for _ in range(2):
+        assert torch.equal(run_decode(small, ws), want_small)
+        assert torch.equal(run_decode(big, ws), want_big)
+    out = torch.empty_like(small.q)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.paged_decode(small.q, small.k_caches[0], small.v_caches[0], small.block_tables,
+                         small.context_lens, 4, 1.0 / math.sqrt(128), small.max_context_len, ws,
+                         out=out)
+    for _ in range(2):
+        graph.replay()
+        assert torch.equal(out, want_small)
+        assert torch.equal(run_decode(big, ws), want_big)
+    del graph
+    assert ops.device_status() == 0
+
+
 def test_general_entry_dispatches_decode(device):
     ctx = np.random.default_rng(12).integers(100, 3000, size=6)
     b = make_decode(LLAMA8B, ctx, torch.bfloat16, device, 12)
