@@ -667,9 +667,10 @@ def run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, ba
     """Head-sharded decode of ONE C2 batch (64 sequences, 32 layers) over all ranks: rank r holds
     KV heads [8r/N, 8(r+1)/N) of every layer's pool and the matching query heads (strong
     scaling). Fused: fa_paged_decode_tp stores each rank's head outputs into every rank's output
-    buffer over NVLink, then fa_tp_wait; NCCL: fa_paged_decode into a local buffer followed by
+    buffer over NVLink, then fa_tp_sync; NCCL: fa_paged_decode into a local buffer followed by
     all_gather_into_tensor. Both steps are CUDA graphs of the 32 layers; after either one every
-    rank holds the full [64, 32, 128] output of every layer."""
+    rank holds the full [64, 32, 128] output of every layer. `local` (the rank's decode alone,
+    no exchange) is the floor both are measured against."""
     import torch.distributed as dist
     from flour_b200.tp import HeadShardedGroup, head_shard, torch_exchange
     from flour_b200.workloads import LLAMA8B, Heads, c2_contexts, make_decode
@@ -697,6 +698,11 @@ def run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, ba
             grp.decode(qs[l], b.k_caches[l], b.v_caches[l], b.block_tables, b.context_lens,
                        hs.n_rep, scale, b.max_context_len, ws)
 
+    def step_local():
+        for l in range(NUM_LAYERS):
+            ops.paged_decode(qs[l], b.k_caches[l], b.v_caches[l], b.block_tables, b.context_lens,
+                             hs.n_rep, scale, b.max_context_len, ws, out=loc[l])
+
     def step_nccl():
         for l in range(NUM_LAYERS):
             ops.paged_decode(qs[l], b.k_caches[l], b.v_caches[l], b.block_tables, b.context_lens,
@@ -709,7 +715,7 @@ def run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, ba
                                    * NUM_LAYERS / 1e9, 3)}
     graphs = {}
     try:
-        for name, fn in (("fused", step_fused), ("nccl", step_nccl)):
+        for name, fn in (("local", step_local), ("fused", step_fused), ("nccl", step_nccl)):
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()

@@ -65,6 +65,7 @@ class FaQkvWeights(ctypes.Structure):
 _WP = ctypes.POINTER(FaQkvWeights)
 
 FA_MAX_TP = 8
+FA_TP_PUBLISH, FA_TP_WAIT = 1, 2
 
 
 class FaIpcHandle(ctypes.Structure):
@@ -81,7 +82,6 @@ class FaTpGroup(ctypes.Structure):
         ("rank", ctypes.c_int32),
         ("out", ctypes.c_void_p * FA_MAX_TP),
         ("flags", ctypes.c_void_p * FA_MAX_TP),
-        ("done_counter", ctypes.c_void_p),
         ("epoch_counter", ctypes.c_void_p),
     ]
 
@@ -111,9 +111,9 @@ SIGNATURES = {
     "fa_ipc_free": (_I32, [_P]),
     "fa_ipc_open": (_I32, [_HP, ctypes.POINTER(_P)]),
     "fa_ipc_close": (_I32, [_P]),
-    "fa_paged_decode_tp": (_I32, [_GP, _LP, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F,
-                                  ctypes.c_uint32, _P, _SZ, _P]),
-    "fa_tp_wait": (_I32, [_GP, ctypes.c_uint32, _I64, _P]),
+    "fa_paged_decode_tp": (_I32, [_GP, _LP, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P,
+                                  _SZ, _P]),
+    "fa_tp_sync": (_I32, [_GP, ctypes.c_uint32, _I32, _I64, _P]),
 }
 
 

@@ -30,9 +30,10 @@
 // Head-sharded groups (tensor parallel over KV heads, one GPU per rank). The final write of each
 // (sequence, kv head) goes to every rank's output buffer (peer memory over NVLink, mapped by
 // CUDA IPC) at the rank's head offset, so the all-gather of the per-head outputs happens inside
-// the kernel. After its writes, each (sequence, kv head) bumps a done counter (system-scope fence
-// first); the last one publishes `epoch` into every rank's flag slot for this rank with a
-// system-scope release store. Consumers wait for all ranks' flags (fa_tp_wait).
+// the kernel, overlapped with the attention of the other heads. Completion is signalled by the
+// next launch on the stream (tp_sync_kernel): stream order makes every store of this kernel
+// complete before it publishes an epoch flag to the other ranks, so the decode kernel itself
+// carries no fences or counters.
 #pragma once
 
 #include "fa_common.cuh"
@@ -47,13 +48,9 @@ struct DecodeParams {
   // Head-sharded mode (n_outs > 0): outs[r] = rank r's [num_seqs, out_heads, HD] buffer; this
   // rank's heads start at out_head0. Otherwise out / num_heads / head 0.
   void *outs[kMaxTp];
-  uint32_t *flag_slots[kMaxTp];  // &flags_of_rank_r[this rank]
-  int32_t *done_counter;         // back to 0 after every launch
-  uint32_t *epoch_counter;       // device epoch, advanced by the launch when epoch == 0
   int32_t n_outs;
   int32_t out_heads;
   int32_t out_head0;
-  uint32_t epoch;
   const int32_t *context_lens;   // [num_seqs]
   const int32_t *block_tables;   // [num_seqs, max_blocks_per_seq]
   float *part_o;                 // [num_seqs, num_heads, max_splits, HD]
@@ -108,34 +105,6 @@ __device__ __forceinline__ void store_out(const DecodeParams &p, int b, int hq, 
   for (int r = 0; r < p.n_outs; ++r) static_cast<T *>(p.outs[r])[off] = e;
 }
 
-// Publish epoch e into every rank's flag slot for this rank (after a system-scope fence).
-__device__ __forceinline__ void publish_epoch(uint32_t *const *slots, int n, uint32_t e) {
-  __threadfence_system();
-  for (int r = 0; r < n; ++r)
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slots[r]), "r"(e) : "memory");
-}
-
-// The epoch a launch publishes: the host's, or (epoch 0) the next device epoch. Called by the
-// single thread that publishes; launches on one stream run one after the other.
-__device__ __forceinline__ uint32_t next_epoch(uint32_t host_epoch, uint32_t *counter) {
-  if (host_epoch != 0) return host_epoch;
-  const uint32_t e = *counter + 1;
-  *counter = e;
-  return e;
-}
-
-// Called by one thread after this CTA wrote the final output of one (sequence, kv head). In a
-// head-sharded group, the last of them publishes the epoch to every rank.
-__device__ __forceinline__ void output_done(const DecodeParams &p) {
-  if (p.n_outs == 0 || p.done_counter == nullptr) return;
-  __threadfence_system();  // this CTA's peer stores before the count
-  const int total = p.num_seqs * p.num_kv_heads;
-  if (atomicAdd(p.done_counter, 1) == total - 1) {
-    *p.done_counter = 0;   // ready for the next launch (stream order separates launches)
-    publish_epoch(p.flag_slots, p.n_outs, next_epoch(p.epoch, p.epoch_counter));
-  }
-}
-
 template <typename T, int HD, int NSTAGE>
 __global__ void __launch_bounds__(kDecodeThreads, 2)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
@@ -163,8 +132,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       if (tid == 0) report(FA_DEVERR_CONTEXT);
       for (int x = tid; x < n_rep * HD; x += kDecodeThreads)
         store_out<T>(p, b, kvh * n_rep + x / HD, HD, x % HD, 0.f);
-      __syncthreads();
-      if (tid == 0) output_done(p);
     }
     return;
   }
@@ -358,13 +325,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       if (x == 0) p.part_lse[pi] = M + __log2f(Lsum);
     }
   }
-  if (single) {
-    if (p.n_outs) {  // uniform: the whole CTA takes it or not
-      __syncthreads();
-      if (tid == 0) output_done(p);
-    }
-    return;
-  }
+  if (single) return;
 
   // ---- last split of this (sequence, kv_head) merges the partials ------------------------
   __threadfence();
@@ -397,36 +358,50 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     }
     store_out<T>(p, b, hq0 + h, HD, x, O / W);
   }
-  if (p.n_outs) __syncthreads();  // uniform
-  if (tid == 0) {
-    p.counters[b * p.num_kv_heads + kvh] = 0;  // ready for the next launch
-    output_done(p);
-  }
+  if (tid == 0) p.counters[b * p.num_kv_heads + kvh] = 0;  // ready for the next launch
 }
 
-// Head-sharded groups, empty batch: publish `epoch` to every rank without a decode launch.
+// Head-sharded groups: mark this rank's preceding launches on the stream complete and/or wait
+// for the other ranks. Publish (thread 0): epoch e (the host's, or with epoch 0 the next device
+// epoch *counter + 1) goes into slot [rank] of every rank's flag array with a system-scope
+// release. Stream order already completed the preceding decode, its peer stores included.
+// Wait (thread s < tp): poll this rank's flags[s] until it reaches e (wrap-around order; with
+// epoch 0, e = *counter), bounded by device time and an iteration cap; on expiry it reports
+// FA_DEVERR_TIMEOUT and returns.
 struct TpFlagSlots {
   uint32_t *slot[kMaxTp];
 };
-__global__ void tp_publish_kernel(TpFlagSlots slots, int tp, uint32_t epoch, uint32_t *counter) {
-  if (threadIdx.x == 0) publish_epoch(slots.slot, tp, next_epoch(epoch, counter));
-}
+constexpr int kTpPublish = 1, kTpWait = 2;
 
-// Head-sharded groups: one thread per rank polls flags[s] (stored by rank s over NVLink) until
-// it reaches `epoch` (wrap-around order; 0 = this rank's device epoch). Bounded by device time
-// and by an iteration cap; on expiry it reports FA_DEVERR_TIMEOUT and returns.
-__global__ void tp_wait_kernel(const uint32_t *flags, int tp, uint32_t epoch,
-                               const uint32_t *counter, unsigned long long timeout_ns) {
+__global__ void tp_sync_kernel(TpFlagSlots publish_to, const uint32_t *my_flags, int tp,
+                               uint32_t epoch, uint32_t *counter, int mode,
+                               unsigned long long timeout_ns) {
+  __shared__ uint32_t s_epoch;
   const int s = threadIdx.x;
-  if (s >= tp) return;
-  if (epoch == 0) epoch = *counter;
+  if (s == 0) {
+    uint32_t e = epoch;
+    if (e == 0) {
+      e = *counter + ((mode & kTpPublish) ? 1u : 0u);
+      if (mode & kTpPublish) *counter = e;
+    }
+    if (mode & kTpPublish) {
+      __threadfence_system();
+      for (int r = 0; r < tp; ++r)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(publish_to.slot[r]), "r"(e)
+                     : "memory");
+    }
+    s_epoch = e;
+  }
+  __syncthreads();
+  if (!(mode & kTpWait) || s >= tp) return;
+  const uint32_t e = s_epoch;
   unsigned long long t0, t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   const unsigned long long max_iters = timeout_ns / 64 + 4096;  // sleeps are >= ~100 ns
   for (unsigned long long it = 0;; ++it) {
     uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
-    if (int32_t(v - epoch) >= 0) return;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(my_flags + s) : "memory");
+    if (int32_t(v - e) >= 0) return;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     if (t - t0 > timeout_ns || it >= max_iters) {
       report(FA_DEVERR_TIMEOUT);

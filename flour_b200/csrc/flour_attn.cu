@@ -201,16 +201,10 @@ fa_status zero_stale_tickets(void *ws, size_t ticket_bytes, cudaStream_t stream)
   return FA_OK;
 }
 
-// Head-sharded output targets of one decode call (NULL: plain single-GPU output).
-struct TpTargets {
-  const fa_tp_group *group;
-  uint32_t epoch;
-};
-
 fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const int32_t *ctx,
                         const int32_t *tables, int max_blocks, int num_seqs, int num_heads,
                         int n_rep, int max_context_len, float scale, void *ws, size_t ws_bytes,
-                        cudaStream_t stream, const TpTargets *tpt = nullptr,
+                        cudaStream_t stream, const fa_tp_group *tp = nullptr,
                         bool caller_workspace = true) {
   DecodePlan plan;
   if (!plan_decode(num_seqs, L->num_kv_heads, max_context_len, &plan))
@@ -245,18 +239,11 @@ fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const in
   p.max_splits = plan.max_splits;
   p.max_context_len = max_context_len;
   p.scale_log2 = scale * 1.4426950408889634f;
-  if (tpt) {
-    const fa_tp_group *g = tpt->group;
-    p.n_outs = g->tp;
-    p.out_heads = g->tp * num_heads;
-    p.out_head0 = g->rank * num_heads;
-    p.epoch = tpt->epoch;
-    p.done_counter = g->done_counter;
-    p.epoch_counter = g->epoch_counter;
-    for (int r = 0; r < g->tp; ++r) {
-      p.outs[r] = g->out[r];
-      p.flag_slots[r] = g->flags[r] + g->rank;
-    }
+  if (tp) {  // head-sharded: every rank's buffer, at this rank's head offset
+    p.n_outs = tp->tp;
+    p.out_heads = tp->tp * num_heads;
+    p.out_head0 = tp->rank * num_heads;
+    for (int r = 0; r < tp->tp; ++r) p.outs[r] = tp->out[r];
   }
   const int64_t rows = int64_t(L->num_blocks) * L->num_kv_heads * L->block_size;
   CUtensorMap tk, tv;
@@ -949,49 +936,44 @@ static fa_status check_tp_group(const fa_tp_group *g, const char *who) {
 fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer, const void *query,
                              const int32_t *context_lens, const int32_t *block_tables,
                              int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
-                             int32_t n_rep, int32_t max_context_len, float scale, uint32_t epoch,
-                             void *workspace, size_t workspace_bytes, fa_stream_t stream) {
+                             int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
+                             size_t workspace_bytes, fa_stream_t stream) {
   const char *who = "paged_decode_tp";
   if (fa_status s = check_tp_group(group, who); s != FA_OK) return s;
-  if (epoch == 0 && !group->epoch_counter)
-    return fail(FA_EINVAL, "%s: epoch 0 (device epochs) needs group->epoch_counter", who);
   for (int r = 0; r < group->tp; ++r)
     if (!group->out[r] || !aligned(group->out[r], 16))
       return fail(FA_EINVAL, "%s: out[%d] is NULL or not 16-byte aligned", who, r);
-  if (!group->done_counter) return fail(FA_EINVAL, "%s: done_counter is NULL", who);
   if (fa_status s = check_attention_args(who, layer, query, group->out[group->rank], context_lens,
                                          block_tables, max_blocks_per_seq, num_seqs, num_heads,
                                          n_rep, max_context_len, scale);
       s != FA_OK)
     return s;
-  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (num_seqs == 0) {  // nothing to write; the peers still wait for this epoch
-    fa::TpFlagSlots slots{};
-    for (int r = 0; r < group->tp; ++r) slots.slot[r] = group->flags[r] + group->rank;
-    fa::tp_publish_kernel<<<1, 32, 0, st>>>(slots, group->tp, epoch, group->epoch_counter);
-    return check_launch(who);
-  }
+  if (num_seqs == 0) return ok();
   if (max_context_len < 1) return fail(FA_ERANGE, "%s: max_context_len must be >= 1", who);
   if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "%s: more than 65535 sequences per call", who);
   if (!decode_fast_path(layer, n_rep, query, group->out[group->rank]))
     return fail(FA_EUNSUPPORTED,
                 "%s: needs a 16-bit pool, block_size 16, head_dim 64/128, n_rep <= 8 and "
                 "16-byte aligned buffers", who);
-  const TpTargets tpt{group, epoch};
   return launch_decode(layer, query, nullptr, context_lens, block_tables, max_blocks_per_seq,
                        num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
-                       workspace_bytes, st, &tpt);
+                       workspace_bytes, reinterpret_cast<cudaStream_t>(stream), group);
 }
 
-fa_status fa_tp_wait(const fa_tp_group *group, uint32_t epoch, int64_t timeout_ns, fa_stream_t stream) {
-  const char *who = "tp_wait";
+fa_status fa_tp_sync(const fa_tp_group *group, uint32_t epoch, int32_t mode, int64_t timeout_ns,
+                     fa_stream_t stream) {
+  const char *who = "tp_sync";
   if (fa_status s = check_tp_group(group, who); s != FA_OK) return s;
+  if (mode < 1 || mode > (FA_TP_PUBLISH | FA_TP_WAIT))
+    return fail(FA_EINVAL, "%s: mode %d (FA_TP_PUBLISH, FA_TP_WAIT or both)", who, mode);
   if (epoch == 0 && !group->epoch_counter)
     return fail(FA_EINVAL, "%s: epoch 0 (device epochs) needs group->epoch_counter", who);
-  if (timeout_ns < 1000 || timeout_ns > 10000000000LL)
+  if ((mode & FA_TP_WAIT) && (timeout_ns < 1000 || timeout_ns > 10000000000LL))
     return fail(FA_ERANGE, "%s: timeout_ns %lld outside [1e3, 1e10]", who, (long long)timeout_ns);
-  fa::tp_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      group->flags[group->rank], group->tp, epoch, group->epoch_counter,
+  fa::TpFlagSlots slots{};
+  for (int r = 0; r < group->tp; ++r) slots.slot[r] = group->flags[r] + group->rank;
+  fa::tp_sync_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      slots, group->flags[group->rank], group->tp, epoch, group->epoch_counter, mode,
       (unsigned long long)timeout_ns);
   return check_launch(who);
 }

@@ -5,8 +5,8 @@ src/models/common/attention.rs:104-109) and never shards heads; this optional mo
 models whose pool does not fit one GPU or whose per-token latency must drop below one GPU's.
 Rank r holds KV heads [r*kv/tp, (r+1)*kv/tp) of every block and query heads
 [r*hq/tp, (r+1)*hq/tp). ``fa_paged_decode_tp`` writes each rank's head outputs straight into
-every rank's output buffer over NVLink (CUDA IPC mappings), then publishes an epoch flag;
-``fa_tp_wait`` makes the consumer's stream wait for all ranks' flags (bounded). So after
+every rank's output buffer over NVLink (CUDA IPC mappings); ``fa_tp_sync`` then publishes an
+epoch flag to every rank and makes the stream wait (bounded) for all ranks' flags. So after
 ``HeadShardedGroup.decode`` every rank holds the full [num_seqs, num_heads, head_dim] output
 that a single-GPU decode produces, with no separate all-gather launch.
 
@@ -14,14 +14,15 @@ Memory of one rank (one cudaMalloc, one IPC handle; the same layout on every ran
     [0, S)            output buffer of odd epochs   [max_seqs, num_heads, head_dim]
     [S, 2S)           output buffer of even epochs
     [2S, 2S+32)       flag array, FA_MAX_TP u32: slot s = last epoch rank s published here
-    [2S+256, +4)      done counter of this rank's decode launches
-    [2S+260, +4)      device epoch of this rank (advanced by each decode launch)
-with S the output size rounded up to 256 bytes. Two output buffers alternate by epoch parity so
-that a rank one epoch ahead never overwrites what a slower peer is still reading.
+    [2S+256, +4)      device epoch of this rank (advanced by each publish)
+with S the output size rounded up to 256 bytes. Two output buffers alternate by decode parity so
+that a rank one decode ahead never overwrites what a slower peer is still reading; this needs a
+sync (publish + wait) after every decode, which ``decode`` does unless told not to, and then
+``sync`` must come before the next ``decode``.
 
-Epochs are counted on the device (``fa_paged_decode_tp`` with epoch 0), so a sequence of
-``decode`` calls can be captured in a CUDA graph and replayed; the host counts calls only to
-pick the output buffer, so a captured sequence should hold an even number of calls.
+Epochs are counted on the device (``fa_tp_sync`` with epoch 0), so a sequence of ``decode``
+calls can be captured in a CUDA graph and replayed; the host counts calls only to pick the
+output buffer, so a captured sequence should hold an even number of calls.
 """
 
 from __future__ import annotations
@@ -32,7 +33,7 @@ from typing import Callable, Sequence
 import torch
 
 from . import _lib
-from ._lib import FA_MAX_TP, FaIpcHandle, FaKvLayer, FaTpGroup, FlourAttnError, check
+from ._lib import FA_MAX_TP, FA_TP_PUBLISH, FA_TP_WAIT, FaIpcHandle, FaTpGroup, FlourAttnError, check
 
 DEFAULT_TIMEOUT_NS = 2_000_000_000
 
@@ -60,8 +61,8 @@ class _Layout:
         self.out_bytes = max_seqs * num_heads * head_dim * elem
         self.stride = _r256(self.out_bytes)
         self.flags_off = 2 * self.stride
-        self.counter_off = self.flags_off + 256
-        self.total = self.counter_off + 256
+        self.epoch_off = self.flags_off + 256
+        self.total = self.epoch_off + 256
 
 
 class _CudaBytes:
@@ -106,7 +107,8 @@ class HeadShardedGroup:
         self.device = torch.device(device if device is not None else "cuda")
         self._lib = lib if lib is not None else _lib.lib()
         self.layout = _Layout(max_seqs, num_heads, head_dim, torch.tensor([], dtype=dtype).element_size())
-        self.epoch = 0
+        self.epoch = 0          # decodes so far (= the device epoch once each is synced)
+        self._pending = False   # a decode without its sync
         self._bases: list[int] = [0] * tp
         self._opened: list[int] = []
         ptr, handle = ctypes.c_void_p(), FaIpcHandle()
@@ -140,8 +142,7 @@ class HeadShardedGroup:
         for r in range(self.tp):
             g.out[r] = self._bases[r] + off
             g.flags[r] = self._bases[r] + self.layout.flags_off
-        g.done_counter = self._local + self.layout.counter_off
-        g.epoch_counter = self._local + self.layout.counter_off + 4
+        g.epoch_counter = self._local + self.layout.epoch_off
         return g
 
     def group_for(self, epoch: int) -> FaTpGroup:
@@ -161,9 +162,12 @@ class HeadShardedGroup:
                max_context_len: int, workspace=None, wait: bool = True,
                timeout_ns: int = DEFAULT_TIMEOUT_NS, stream=None) -> torch.Tensor:
         """Decode this rank's heads (query [B, num_heads/tp, d], k/v_cache holding this rank's KV
-        heads) into every rank's output; with `wait`, also wait for the other ranks and return
-        the full [B, num_heads, d] output. Every rank calls it the same number of times."""
+        heads) into every rank's output and return the full [B, num_heads, d] output view. With
+        `wait` (the default) the sync follows at once; otherwise call ``sync`` before reading the
+        output or decoding again. Every rank makes the same calls."""
         from . import ops
+        if self._pending:
+            raise FlourAttnError(_lib.FA_EINVAL, "decode: the previous decode has not been synced")
         layer = ops.layer_desc(k_cache, v_cache)
         query = query.contiguous()
         B, hq, d = query.shape
@@ -176,23 +180,25 @@ class HeadShardedGroup:
         bt, cl = ops._i32(block_tables, "block_tables"), ops._i32(context_lens, "context_lens")
         need = ops.workspace_size(max(B, 1), hq, k_cache.shape[1], d, max(max_context_len, 1), 1)
         wp, wn = ops._ws_args(workspace, need)
-        epoch = self.epoch + 1  # the device epoch this launch publishes (all ranks in lockstep)
+        epoch = self.epoch + 1  # the device epoch its sync publishes (all ranks in lockstep)
         g = self.group_for(epoch)
         check(self._lib.fa_paged_decode_tp(ctypes.byref(g), ctypes.byref(layer), ops._ptr(query),
                                            ops._ptr(cl), ops._ptr(bt), bt.shape[1], B, hq, n_rep,
-                                           max_context_len, scale, 0, wp, wn,
-                                           ops._stream(stream)), "paged_decode_tp")
+                                           max_context_len, scale, wp, wn, ops._stream(stream)),
+              "paged_decode_tp")
         self.epoch = epoch
+        self._pending = True
         if wait:
-            self.wait(None, timeout_ns, stream)
+            self.sync(timeout_ns, stream)
         return self.output(epoch, B)
 
-    def wait(self, epoch: int | None = None, timeout_ns: int = DEFAULT_TIMEOUT_NS, stream=None) -> None:
-        """Make `stream` wait (bounded) until every rank published `epoch`; None waits for this
-        rank's current device epoch (the one its last decode published)."""
+    def sync(self, timeout_ns: int = DEFAULT_TIMEOUT_NS, stream=None) -> None:
+        """Publish this rank's last decode to every rank and make `stream` wait (bounded) until
+        every rank published it (device-counted epochs)."""
         from . import ops
-        check(self._lib.fa_tp_wait(ctypes.byref(self._groups[0]), 0 if epoch is None else epoch,
-                                   timeout_ns, ops._stream(stream)), "tp_wait")
+        check(self._lib.fa_tp_sync(ctypes.byref(self._groups[0]), 0, FA_TP_PUBLISH | FA_TP_WAIT,
+                                   timeout_ns, ops._stream(stream)), "tp_sync")
+        self._pending = False
 
     def close(self) -> None:
         """Unmap the peers and free this rank's buffers (after all GPU work that uses them)."""

@@ -253,17 +253,18 @@ FA_API fa_status fa_o_proj_residual(const void *attn, const void *weight, const 
  * kernel writes each finished (sequence, kv head) output into EVERY rank's output buffer at the
  * rank's head offset (stores into peer memory over NVLink, mapped with CUDA IPC), so the
  * all-gather of the head outputs is part of the attention kernel, with no separate collective.
- * The kernel's last CTA then stores `epoch` into slot [rank] of every rank's flag array
- * (system-scope release); fa_tp_wait makes a stream wait (bounded) until all ranks published
- * the epoch into this rank's flags.
+ * fa_tp_sync then publishes an epoch into slot [rank] of every rank's flag array (system-scope
+ * release; stream order has completed the decode's stores) and waits, bounded, until every rank
+ * published it into this rank's flags.
  *
- * Buffers: every rank allocates its output buffers, a flag array of FA_MAX_TP u32 and a done
- * counter with fa_ipc_alloc (zero-filled), exchanges the handles, and opens its peers'
- * handles with fa_ipc_open. Epochs start at 1 and grow by one per call. A rank may publish
- * epoch e+1 into a peer before that peer waited for epoch e, so the group alternates two
- * output buffers by epoch parity: the buffer of epoch e is rewritten at epoch e+2, which every
- * rank starts only after fa_tp_wait(e+1), i.e. after each peer enqueued its uses of epoch e's
- * output ahead of its decode of epoch e+1 on the same stream. */
+ * Protocol: every rank makes the same calls, each fa_paged_decode_tp followed on the same
+ * stream by fa_tp_sync(FA_TP_PUBLISH | FA_TP_WAIT) before the rank's next fa_paged_decode_tp
+ * and before anything reads the output. Buffers: every rank allocates two output buffers, a flag
+ * array of FA_MAX_TP u32 and an epoch counter with fa_ipc_alloc (zero-filled), exchanges the
+ * handles and opens its peers' handles with fa_ipc_open. Consecutive decodes alternate the two
+ * output buffers (two fa_tp_group values): a rank can be one decode ahead of a slower peer, and
+ * the buffer of decode k is rewritten by decode k+2 only after every peer's sync k+1, i.e. after
+ * each peer enqueued its reads of decode k's output ahead of its decode k+1. */
 #define FA_MAX_TP 8
 typedef struct fa_ipc_handle {
   unsigned char bytes[64]; /* cudaIpcMemHandle_t */
@@ -282,32 +283,31 @@ typedef struct fa_tp_group {
   void *out[FA_MAX_TP];        /* rank r's output buffer [num_seqs, tp*num_heads, head_dim] for
                                   this call, as mapped in this process; 16-byte aligned */
   uint32_t *flags[FA_MAX_TP];  /* rank r's flag array (FA_MAX_TP u32), as mapped here */
-  int32_t *done_counter;       /* this rank's own counter (4 bytes, zero, device memory) */
   uint32_t *epoch_counter;     /* this rank's device epoch (4 bytes, zero): used when epoch == 0 */
 } fa_tp_group;
 
 /* fa_paged_decode over this rank's head shard (layer = the rank's KV heads, query [num_seqs,
  * num_heads, head_dim] = its query heads), writing the rows into every rank's group->out at
- * head offset rank*num_heads, then publishing the epoch. Requires the fast decode path (16-bit
- * pool, block_size 16, head_dim 64/128, n_rep <= 8). Does not wait.
- * epoch >= 1: publish that value (the host counts epochs).
- * epoch == 0: the kernel adds one to *group->epoch_counter and publishes the result, so the
- *   calls can be captured in a CUDA graph and replayed (every rank must make the same calls;
- *   a captured sequence should hold an even number of calls so that the output buffers keep
- *   alternating across replays). Use one of the two modes per group. */
+ * head offset rank*num_heads. Requires the fast decode path (16-bit pool, block_size 16,
+ * head_dim 64/128, n_rep <= 8). Signals nothing: fa_tp_sync follows it. */
 FA_API fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer,
                                     const void *query, const int32_t *context_lens,
                                     const int32_t *block_tables, int32_t max_blocks_per_seq,
                                     int32_t num_seqs, int32_t num_heads, int32_t n_rep,
-                                    int32_t max_context_len, float scale, uint32_t epoch,
-                                    void *workspace, size_t workspace_bytes, fa_stream_t stream);
+                                    int32_t max_context_len, float scale, void *workspace,
+                                    size_t workspace_bytes, fa_stream_t stream);
 
-/* Make `stream` wait until every rank published `epoch` (or a later one) into this rank's
- * flags; epoch 0 means this rank's current device epoch (*group->epoch_counter, read when the
- * wait starts). The wait gives up after timeout_ns (1 us .. 10 s) of device time, sets
- * FA_DEVERR_TIMEOUT (fa_device_status) and returns, leaving the context usable. */
-FA_API fa_status fa_tp_wait(const fa_tp_group *group, uint32_t epoch, int64_t timeout_ns,
-                            fa_stream_t stream);
+/* FA_TP_PUBLISH: store the epoch into every rank's flag slot [group->rank]; FA_TP_WAIT: make
+ * `stream` wait until every rank's slot in this rank's flags holds the epoch (or a later one).
+ * epoch >= 1: that value (the host counts epochs). epoch == 0: device-counted, so the calls can
+ * be captured in a CUDA graph and replayed: a publish first adds one to *group->epoch_counter,
+ * and the epoch is the counter's value. Use one kind of epoch per group. The wait gives up
+ * after timeout_ns (1 us .. 10 s) of device time, sets FA_DEVERR_TIMEOUT (fa_device_status)
+ * and returns, leaving the context usable. */
+#define FA_TP_PUBLISH 1
+#define FA_TP_WAIT 2
+FA_API fa_status fa_tp_sync(const fa_tp_group *group, uint32_t epoch, int32_t mode,
+                            int64_t timeout_ns, fa_stream_t stream);
 
 #ifdef __cplusplus
 }

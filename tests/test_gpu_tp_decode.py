@@ -1,14 +1,15 @@
-"""Head-sharded decode (fa_paged_decode_tp + fa_tp_wait) on the GPU.
+"""Head-sharded decode (fa_paged_decode_tp + fa_tp_sync) on the GPU.
 
-The kernel writes each rank's head outputs into every rank's output buffer and publishes an
-epoch flag; after fa_tp_wait every rank holds the full decode output. Checked here:
+The kernel writes each rank's head outputs into every rank's output buffer; fa_tp_sync publishes
+an epoch flag to every rank and waits for all of them, after which every rank holds the full
+decode output. Checked here:
   * tp = 1 through HeadShardedGroup: bit-identical to fa_paged_decode (same kernel, same plan),
     over several epochs (both output buffers of the parity scheme);
-  * tp = 2 and 4 emulated in one process on one GPU (every rank's buffers local, decodes run one
-    after the other on one stream, so no launch waits for another one): every rank's buffer
-    equals the oracle, including a sequence with an empty context (zeros + FA_DEVERR_CONTEXT,
-    flags still published);
-  * a wait for an epoch nobody publishes ends after its time limit with FA_DEVERR_TIMEOUT and
+  * tp = 2 and 4 emulated in one process on one GPU (every rank's buffers local; all decodes and
+    publishes run one after the other on one stream before any wait, so no launch waits for a
+    later one): every rank's buffer equals the oracle, including a sequence with an empty context
+    (zeros + FA_DEVERR_CONTEXT);
+  * a wait for a rank that never publishes ends after its time limit with FA_DEVERR_TIMEOUT and
     leaves the context usable;
   * with >= 2 GPUs: two processes, one GPU each, buffers mapped with CUDA IPC, the stores cross
     NVLink (skipped on a one-GPU box).
@@ -109,11 +110,10 @@ def test_tp_group_replays_in_a_cuda_graph(device):
 
 
 def local_groups(tp, num_seqs, num_heads, head_dim, device):
-    """tp groups whose buffers all live on this GPU (rank r's out/flags/counter tensors)."""
+    """tp groups whose buffers all live on this GPU (rank r's out and flags tensors)."""
     outs = [torch.zeros((num_seqs, num_heads, head_dim), dtype=torch.bfloat16, device=device)
             for _ in range(tp)]
     flags = [torch.zeros(_lib.FA_MAX_TP, dtype=torch.int32, device=device) for _ in range(tp)]
-    counters = [torch.zeros(1, dtype=torch.int32, device=device) for _ in range(tp)]
     groups = []
     for rank in range(tp):
         g = _lib.FaTpGroup()
@@ -121,9 +121,8 @@ def local_groups(tp, num_seqs, num_heads, head_dim, device):
         for r in range(tp):
             g.out[r] = outs[r].data_ptr()
             g.flags[r] = flags[r].data_ptr()
-        g.done_counter = counters[rank].data_ptr()
         groups.append(g)
-    return groups, outs, flags, counters
+    return groups, outs, flags
 
 
 @pytest.mark.parametrize("tp,heads", [(2, LLAMA8B), (4, LLAMA8B), (4, QWEN7B)])
@@ -132,7 +131,7 @@ def test_tp_emulated_on_one_gpu(device, tp, heads):
     b = make_decode(h, c2_contexts(40 + tp, batch=12), torch.bfloat16, device, 40 + tp)
     cl = b.context_lens.clone()
     cl[3] = 0  # empty context: zero output, FA_DEVERR_CONTEXT, flags still published
-    groups, outs, flags, counters = local_groups(tp, b.num_seqs, h.num_heads, h.head_dim, device)
+    groups, outs, flags = local_groups(tp, b.num_seqs, h.num_heads, h.head_dim, device)
     lib = _lib.lib()
     scale = 1.0 / math.sqrt(h.head_dim)
     ws = [ops.Workspace(device) for _ in range(tp)]
@@ -148,16 +147,17 @@ def test_tp_emulated_on_one_gpu(device, tp, heads):
                                               ops._ptr(q), ops._ptr(cl),
                                               ops._ptr(b.block_tables), b.block_tables.shape[1],
                                               b.num_seqs, q.shape[1], h.n_rep, b.max_context_len,
-                                              scale, epoch, wp, wn, stream), "paged_decode_tp")
+                                              scale, wp, wn, stream), "paged_decode_tp")
+            _lib.check(lib.fa_tp_sync(ctypes.byref(groups[rank]), epoch, _lib.FA_TP_PUBLISH, 0,
+                                      stream), "tp_sync publish")
         for rank in range(tp):
-            _lib.check(lib.fa_tp_wait(ctypes.byref(groups[rank]), epoch, 10_000_000, stream),
-                       "tp_wait")
+            _lib.check(lib.fa_tp_sync(ctypes.byref(groups[rank]), epoch, _lib.FA_TP_WAIT,
+                                      10_000_000, stream), "tp_sync wait")
         torch.cuda.synchronize()
         status = ops.device_status()
         assert status == _lib.FA_DEVERR_CONTEXT, hex(status)
         for r in range(tp):
             assert flags[r][:tp].tolist() == [epoch] * tp
-            assert counters[r].item() == 0
     want = full_oracle(b)
     keep = [i for i in range(b.num_seqs) if i != 3]
     for r in range(tp):
@@ -168,14 +168,19 @@ def test_tp_emulated_on_one_gpu(device, tp, heads):
 
 
 def test_wait_times_out_and_context_survives(device):
+    # Rank 0 of an emulated pair publishes and waits; rank 1 never publishes, so the wait ends
+    # after its 1 ms limit with FA_DEVERR_TIMEOUT. The context stays usable afterwards.
     h = LLAMA8B
+    groups, *_ = local_groups(2, 4, h.num_heads, h.head_dim, device)
+    lib = _lib.lib()
+    assert ops.device_status() == 0
+    _lib.check(lib.fa_tp_sync(ctypes.byref(groups[0]), 1, _lib.FA_TP_PUBLISH | _lib.FA_TP_WAIT,
+                              1_000_000, ops._stream()), "tp_sync")
+    torch.cuda.synchronize()
+    assert ops.device_status() == _lib.FA_DEVERR_TIMEOUT
+    b = make_decode(h, np.array([100, 2000, 17, 5]), torch.bfloat16, device, 3)
     grp = HeadShardedGroup(1, 0, 4, h.num_heads, h.head_dim, torch.bfloat16, lambda x: [x], device)
     try:
-        assert ops.device_status() == 0
-        grp.wait(epoch=7, timeout_ns=1_000_000)  # nothing publishes epoch 7
-        torch.cuda.synchronize()
-        assert ops.device_status() == _lib.FA_DEVERR_TIMEOUT
-        b = make_decode(h, np.array([100, 2000, 17, 5]), torch.bfloat16, device, 3)
         got = grp.decode(b.q, b.k_caches[0], b.v_caches[0], b.block_tables, b.context_lens,
                          h.n_rep, 1.0 / math.sqrt(h.head_dim), b.max_context_len,
                          ops.Workspace(device))
@@ -187,25 +192,41 @@ def test_wait_times_out_and_context_survives(device):
         grp.close()
 
 
-def test_tp_rejects_bad_groups(device):
+def test_tp_rejects_bad_groups_and_unsynced_decodes(device):
     h = LLAMA8B
     groups, *_ = local_groups(2, 4, h.num_heads, h.head_dim, device)
     lib = _lib.lib()
     g = groups[0]
+    both = _lib.FA_TP_PUBLISH | _lib.FA_TP_WAIT
     g.rank = 2
-    assert lib.fa_tp_wait(ctypes.byref(g), 1, 1_000_000, None) == _lib.FA_EINVAL
+    assert lib.fa_tp_sync(ctypes.byref(g), 1, both, 1_000_000, None) == _lib.FA_EINVAL
     g.rank = 0
-    assert lib.fa_tp_wait(ctypes.byref(g), 0, 1_000_000, None) == _lib.FA_EINVAL
-    assert lib.fa_tp_wait(ctypes.byref(g), 1, 10, None) == _lib.FA_ERANGE
+    assert lib.fa_tp_sync(ctypes.byref(g), 0, both, 1_000_000, None) == _lib.FA_EINVAL  # no counter
+    assert lib.fa_tp_sync(ctypes.byref(g), 1, both, 10, None) == _lib.FA_ERANGE
+    assert lib.fa_tp_sync(ctypes.byref(g), 1, 4, 1_000_000, None) == _lib.FA_EINVAL
     g.out[1] = None
     b = make_decode(h, np.array([64]), torch.bfloat16, device, 1)
     q, kc, vc = shard_batch(b, 2, 0)
     layer = ops.layer_desc(kc, vc)
     st = lib.fa_paged_decode_tp(ctypes.byref(g), ctypes.byref(layer), ops._ptr(q),
                                 ops._ptr(b.context_lens), ops._ptr(b.block_tables), 4, 1,
-                                q.shape[1], h.n_rep, 64, 0.1, 1, None, 0, None)
+                                q.shape[1], h.n_rep, 64, 0.1, None, 0, None)
     assert st == _lib.FA_EINVAL
     assert b"out[1]" in lib.fa_last_error_message()
+    grp = HeadShardedGroup(1, 0, 1, h.num_heads, h.head_dim, torch.bfloat16, lambda x: [x], device)
+    try:
+        args = (b.k_caches[0], b.v_caches[0], b.block_tables, b.context_lens, h.n_rep, 0.1, 64,
+                ops.Workspace(device))
+        grp.decode(b.q, *args, wait=False)
+        with pytest.raises(_lib.FlourAttnError):
+            grp.decode(b.q, *args)  # the first decode was not synced
+        grp.sync()
+        grp.decode(b.q, *args)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+    finally:
+        torch.cuda.synchronize()
+        grp.close()
 
 
 # ---- two processes, one GPU each, CUDA IPC over NVLink ----------------------------------------

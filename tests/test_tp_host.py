@@ -5,8 +5,8 @@
     r * num_heads/tp of every rank's buffer), restated with the oracle: each rank decodes its
     head shard only, places it into a full-size buffer, and the buffers exchanged over gloo
     assemble into exactly the single-rank output, bit for bit;
-  * HeadShardedGroup's handle exchange and the fa_tp_group it builds (buffer offsets by epoch
-    parity, peers' flag arrays, own done counter), with a stand-in for the C library's IPC
+  * HeadShardedGroup's handle exchange and the fa_tp_group it builds (buffer offsets by decode
+    parity, peers' flag arrays, own epoch counter), with a stand-in for the C library's IPC
     calls so no GPU is needed.
 """
 
@@ -127,10 +127,10 @@ def worker(rank, port, results):
         for epoch in (1, 2):
             g = grp.group_for(epoch)
             groups[epoch] = (g.tp, g.rank, [g.out[r] for r in range(WORLD)],
-                             [g.flags[r] for r in range(WORLD)], g.done_counter, g.epoch_counter)
+                             [g.flags[r] for r in range(WORLD)], g.epoch_counter)
         grp.close()
         results.put((rank, "ok", (contract_ok, fake.nbytes, lay.stride, lay.flags_off,
-                                  lay.counter_off, groups, fake.closed, fake.freed)))
+                                  lay.epoch_off, groups, fake.closed, fake.freed)))
         dist.destroy_process_group()
     except Exception as e:
         results.put((rank, "error", f"{type(e).__name__}: {e}\n{traceback.format_exc()[-600:]}"))
@@ -153,17 +153,16 @@ def test_group_host_logic_two_ranks():
     mapped = lambda r, me: base(r) if r == me else base(r) + (1 << 36)
     for rank, (kind, payload) in out.items():
         assert kind == "ok", f"rank {rank}: {payload}"
-        contract_ok, nbytes, stride, flags_off, counter_off, groups, closed, freed = payload
+        contract_ok, nbytes, stride, flags_off, epoch_off, groups, closed, freed = payload
         assert contract_ok, f"rank {rank}: assembled head shards differ from the full decode"
         out_bytes = 10 * 32 * 128 * 2
         assert stride == (out_bytes + 255) // 256 * 256 and flags_off == 2 * stride
-        assert counter_off == flags_off + 256 and nbytes == counter_off + 256
-        for epoch, (tp, grank, outs, flags, counter, epoch_counter) in groups.items():
+        assert epoch_off == flags_off + 256 and nbytes == epoch_off + 256
+        for epoch, (tp, grank, outs, flags, epoch_counter) in groups.items():
             assert (tp, grank) == (WORLD, rank)
             off = 0 if epoch % 2 else stride  # odd epochs use the first buffer
             assert outs == [mapped(r, rank) + off for r in range(WORLD)]
             assert flags == [mapped(r, rank) + flags_off for r in range(WORLD)]
-            assert counter == base(rank) + counter_off
-            assert epoch_counter == counter + 4
+            assert epoch_counter == base(rank) + epoch_off
         assert closed == [mapped(r, rank) for r in range(WORLD) if r != rank]
         assert freed == [base(rank)]
