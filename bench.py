@@ -5,8 +5,10 @@
 Workload ("C2"): Llama-3-8B heads (32 q / 8 kv, head_dim 128),
 block_size 16, 32 layers with their own pools, batch 64, context lengths ~ U[512, 4096],
 bf16 KV ~ N(0,1), shuffled non-contiguous block tables. One step = one decode step of the
-batch: for each of the 32 layers, reshape_and_cache of the 64 new tokens' K/V into their slots,
-then paged decode attention of the 64 queries (attention.rs:104-109 order). Each layer's pool
+batch: for each of the 32 layers, the write of the 64 new tokens' K/V into their slots followed by
+paged decode attention of the 64 queries (attention.rs:104-109 order), both in one launch of
+fa_paged_decode_append (`unfused_step_ms` times the same step as fa_reshape_and_cache +
+fa_paged_decode, two launches per layer). Each layer's pool
 (~0.6 GB) is larger than L2, so no L2 flush is needed between timed iterations.
 
 Metric value: algorithmic KV bytes read per step (sum ctx x Hkv x d x 2 [K,V] x 2 B, plus the
@@ -246,13 +248,20 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     def layer_step(l, q, kn, vn, out):
-        ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], kn, vn, slots)
-        ops.paged_decode(q, batch.k_caches[l], batch.v_caches[l], batch.block_tables,
-                         batch.context_lens, h.n_rep, scale, batch.max_context_len, ws, out=out)
+        ops.paged_decode_append(q, batch.k_caches[l], batch.v_caches[l], kn, vn,
+                                batch.block_tables, batch.context_lens, h.n_rep, scale,
+                                batch.max_context_len, ws, out=out)
 
     def step():
         for l in range(NUM_LAYERS):
             layer_step(l, qs[l], knew[l], vnew[l], outs[l])
+
+    def step_unfused():
+        for l in range(NUM_LAYERS):
+            ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], knew[l], vnew[l], slots)
+            ops.paged_decode(qs[l], batch.k_caches[l], batch.v_caches[l], batch.block_tables,
+                             batch.context_lens, h.n_rep, scale, batch.max_context_len, ws,
+                             out=outs[l])
 
     for _ in range(args.warmup):
         step()
@@ -309,15 +318,31 @@ def run_ours(args):
     dec_ms = []
     for _ in range(max(2, min(args.steps, 5))):
         for l in range(NUM_LAYERS):
-            ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], knew[l], vnew[l], slots)
             evs[l][0].record(stream)
-            ops.paged_decode(qs[l], batch.k_caches[l], batch.v_caches[l], batch.block_tables,
-                             batch.context_lens, h.n_rep, scale, batch.max_context_len, ws,
-                             out=outs[l])
+            layer_step(l, qs[l], knew[l], vnew[l], outs[l])
             evs[l][1].record(stream)
         torch.cuda.synchronize()
         dec_ms += [a.elapsed_time(b) for a, b in evs]
     dec_avg_ms = statistics.mean(dec_ms)
+
+    # ---- the same step as two launches per layer (reshape_and_cache, then decode) -------------
+    graph_u = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_u):
+        step_unfused()
+    for _ in range(3):
+        graph_u.replay()
+    torch.cuda.synchronize()
+    barrier()
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps_u = max(10, args.steps // 4)
+    u0.record(stream)
+    for _ in range(reps_u):
+        graph_u.replay()
+    u1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    unfused_ms = max_over_ranks(u0.elapsed_time(u1)) / reps_u
+    del graph_u
     achieved = bytes_per_layer / (dec_avg_ms / 1e3) / 1e9
     traffic = profile_traffic("paged_decode_c2")
 
@@ -387,7 +412,8 @@ def run_ours(args):
                          "traffic": traffic, "kernel": "paged_decode_kernel<bf16,128,3>",
                          "launch_ms": round(dec_avg_ms, 5), "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": bytes_per_layer},
-            "gpu_launches": 2 * NUM_LAYERS * args.steps,
+            "gpu_launches": NUM_LAYERS * args.steps,
+            "unfused_step_ms": round(unfused_ms, 4),
             "clocks": clk,
         }
         if e2e:
@@ -415,8 +441,9 @@ def run_ours(args):
 def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_step, world,
             barrier, max_over_ranks):
     """Per step: the host hands per-layer q and new k/v (pinned) plus the step's metadata
-    (block tables, context lengths, slot mapping); the library writes the cache, attends and
-    the host reads every layer's output back. Copies run on a side stream, one layer ahead."""
+    (block tables, context lengths); the library writes the cache and attends (one
+    fa_paged_decode_append per layer) and the host reads every layer's output back. Copies run on
+    a side stream, one layer ahead."""
     B = batch.num_seqs
     gen = torch.Generator().manual_seed(7)
     hq = [torch.randn((B, h.num_heads, h.head_dim), generator=gen).to(torch.bfloat16).pin_memory()
@@ -429,14 +456,13 @@ def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_
           for _ in range(NUM_LAYERS)]
     h_bt = batch.block_tables.cpu().pin_memory()
     h_ctx = batch.context_lens.cpu().pin_memory()
-    h_slots = slots.cpu().pin_memory()
-    d_bt, d_ctx, d_slots = (torch.empty_like(x, device=dev) for x in (h_bt, h_ctx, h_slots))
+    d_bt, d_ctx = (torch.empty_like(x, device=dev) for x in (h_bt, h_ctx))
     dq = [torch.empty_like(x, device=dev) for x in hq]
     dk = [torch.empty_like(x, device=dev) for x in hk]
     dv = [torch.empty_like(x, device=dev) for x in hv]
     do = [torch.empty_like(x, device=dev) for x in ho]
     copy = torch.cuda.Stream(device=dev)
-    h2d = sum(x.numel() * x.element_size() for x in (h_bt, h_ctx, h_slots)) + \
+    h2d = sum(x.numel() * x.element_size() for x in (h_bt, h_ctx)) + \
         sum(x.numel() * x.element_size() for x in hq + hk + hv)
     d2h = sum(x.numel() * x.element_size() for x in ho)
 
@@ -446,7 +472,6 @@ def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_
             copy.wait_stream(stream)
             d_bt.copy_(h_bt, non_blocking=True)
             d_ctx.copy_(h_ctx, non_blocking=True)
-            d_slots.copy_(h_slots, non_blocking=True)
             for l in range(NUM_LAYERS):
                 dq[l].copy_(hq[l], non_blocking=True)
                 dk[l].copy_(hk[l], non_blocking=True)
@@ -457,9 +482,9 @@ def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_
         ev_out = []
         for l in range(NUM_LAYERS):
             stream.wait_event(ev_in[l])
-            ops.reshape_and_cache(batch.k_caches[l], batch.v_caches[l], dk[l], dv[l], d_slots)
-            ops.paged_decode(dq[l], batch.k_caches[l], batch.v_caches[l], d_bt, d_ctx, h.n_rep,
-                             scale, batch.max_context_len, ws, out=do[l])
+            ops.paged_decode_append(dq[l], batch.k_caches[l], batch.v_caches[l], dk[l], dv[l],
+                                    d_bt, d_ctx, h.n_rep, scale, batch.max_context_len, ws,
+                                    out=do[l])
             e = torch.cuda.Event()
             e.record(stream)
             ev_out.append(e)
@@ -595,7 +620,8 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
     (ctx ~ LogNormal(ln 1024, 0.8) capped at 8192); about 10 % are new prompts of L ~ U[256, 2048]
     run as prefill, the rest decode one token. The sequences are partitioned longest-first over
     the ranks, so the total work is fixed as N grows (strong scaling). One step = per layer:
-    reshape_and_cache of the new K/V, the decode launch and the prefill launch; each rank owns its
+    the decode sequences' new K/V write + decode (one fa_paged_decode_append launch), the
+    prefill sequences' reshape_and_cache and the prefill launch; each rank owns its
     own pools. KV values are zero-filled (timing only; the kernels' arithmetic does not depend on
     the values)."""
     from flour_b200.workloads import QWEN7B, c5_plan, lpt_partition, make_decode, make_prefill
@@ -613,9 +639,6 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
     dq = torch.randn((B, h.num_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
     dk = torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
     dv = torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
-    bt = db.block_tables.cpu().numpy()
-    last = db.ctx_host.astype(np.int64) - 1
-    dslots = torch.tensor(bt[np.arange(B), last // 16] * 16 + last % 16, dtype=torch.int32, device=dev)
     dout = torch.empty_like(dq)
     pb = make_prefill(h, pf_len[pf], np.zeros(len(pf), np.int64), torch.bfloat16, dev,
                       args.seed + 100 + rank, num_layers=L, fill=False) if pf else None
@@ -625,9 +648,9 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
 
     def step():
         for l in range(L):
-            ops.reshape_and_cache(db.k_caches[l], db.v_caches[l], dk, dv, dslots)
-            ops.paged_decode(dq, db.k_caches[l], db.v_caches[l], db.block_tables, db.context_lens,
-                             h.n_rep, scale, db.max_context_len, ws_d, out=dout)
+            ops.paged_decode_append(dq, db.k_caches[l], db.v_caches[l], dk, dv, db.block_tables,
+                                    db.context_lens, h.n_rep, scale, db.max_context_len, ws_d,
+                                    out=dout)
             if pb is not None:
                 ops.reshape_and_cache(pb.k_caches[l], pb.v_caches[l], pb.key, pb.value,
                                       pb.slot_mapping)

@@ -102,6 +102,8 @@ SIGNATURES = {
     "fa_paged_attention": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                   _I32, _F, _P, _SZ, _P]),
     "fa_paged_decode": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P, _SZ, _P]),
+    "fa_paged_decode_append": (_I32, [_LP, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I32,
+                                      _I32, _I32, _I32, _I32, _F, _P, _SZ, _P]),
     "fa_paged_decode_noalloc": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P]),
     "fa_paged_prefill": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                                 _F, _P, _SZ, _P]),

@@ -27,6 +27,14 @@
 // (sequence, kv_head) to finish (atomic ticket, no waiting) merges them and resets the ticket.
 // Sequences with a single split write the output directly.
 //
+// Fused append (fa_paged_decode_append): the new token of each sequence sits at position
+// ctx - 1, i.e. on the sequence's last page, which exactly one CTA per (sequence, kv head) loads
+// (the last split). That CTA first copies the token's K and V rows of its KV head from the
+// caller's buffers into the pool slot (generic stores, each writer then fences the generic proxy
+// against the async proxy), and only after the CTA barrier that precedes its first TMA load does
+// any page arrive; so the write and the attention over it happen in one launch, in the order
+// of the reference's write_kv followed by paged_attention.
+//
 // Head-sharded groups (tensor parallel over KV heads, one GPU per rank). The final write of each
 // (sequence, kv head) goes to every rank's output buffer (peer memory over NVLink, mapped by
 // CUDA IPC) at the rank's head offset, so the all-gather of the per-head outputs happens inside
@@ -66,6 +74,13 @@ struct DecodeParams {
   int32_t max_splits;
   int32_t max_context_len;       // host bound the split plan was made for
   float scale_log2;              // scale * log2(e)
+  // Fused append (new_k != nullptr): new_k[b*nk_token + h*nk_head + x] is the new token's key of
+  // sequence b, KV head h (same for new_v); it goes to position ctx-1 of k_pool / v_pool.
+  const void *new_k;
+  const void *new_v;
+  int64_t nk_token, nk_head, nv_token, nv_head;
+  void *k_pool;
+  void *v_pool;
 };
 
 constexpr int kDecodeWarps = 4;
@@ -179,9 +194,32 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       tma_load_2d_hint(vdst + hf * S::kHalfBytes, &tm_v, bar, hf * 64, row, policy);
     }
   };
+  // Fused append: the warp that streams the last page (position ctx - 1) first writes the new
+  // token's K/V row of this KV head into it; all of its lanes fence the generic proxy against
+  // the async proxy before lane 0 issues that page's TMA load. When the last page is not among
+  // the warp's first NSTAGE pages, those are issued first so the write overlaps their loads.
+  const bool appender =
+      p.new_k != nullptr && split == n_splits - 1 && warp == (npg - 1) % kDecodeWarps;
+  auto append_row = [&]() {
+    const int id = table[npg - 1];
+    if (uint32_t(id) < uint32_t(p.num_blocks)) {
+      const size_t dst = ((size_t(id) * p.num_kv_heads + kvh) * kPage + (ctx - 1) % kPage) * HD;
+      const T *nk = static_cast<const T *>(p.new_k) + b * p.nk_token + kvh * p.nk_head;
+      const T *nv = static_cast<const T *>(p.new_v) + b * p.nv_token + kvh * p.nv_head;
+#pragma unroll
+      for (int x = lane; x < HD; x += 32) {
+        static_cast<T *>(p.k_pool)[dst + x] = nk[x];
+        static_cast<T *>(p.v_pool)[dst + x] = nv[x];
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    __syncwarp();
+  };
+  if (appender && n_my <= NSTAGE) append_row();
   if (lane == 0) {
     for (int i = 0; i < NSTAGE && i < n_my; ++i) issue(i);
   }
+  if (appender && n_my > NSTAGE) append_row();
 
   // Q^T fragments (B operand, k = head_dim, n = head), constant for the whole kernel.
   uint32_t qb[KSTEPS][2];

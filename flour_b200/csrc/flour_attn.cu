@@ -201,11 +201,17 @@ fa_status zero_stale_tickets(void *ws, size_t ticket_bytes, cudaStream_t stream)
   return FA_OK;
 }
 
+// The new tokens' K/V of a fused append (fa_paged_decode_append).
+struct AppendArgs {
+  const void *key, *value;
+  int64_t k_token, k_head, v_token, v_head;  // strides in elements
+};
+
 fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const int32_t *ctx,
                         const int32_t *tables, int max_blocks, int num_seqs, int num_heads,
                         int n_rep, int max_context_len, float scale, void *ws, size_t ws_bytes,
                         cudaStream_t stream, const fa_tp_group *tp = nullptr,
-                        bool caller_workspace = true) {
+                        bool caller_workspace = true, const AppendArgs *app = nullptr) {
   DecodePlan plan;
   if (!plan_decode(num_seqs, L->num_kv_heads, max_context_len, &plan))
     return fail(FA_EUNSUPPORTED, "decode: context of %d tokens needs more than %d splits",
@@ -244,6 +250,16 @@ fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const in
     p.out_heads = tp->tp * num_heads;
     p.out_head0 = tp->rank * num_heads;
     for (int r = 0; r < tp->tp; ++r) p.outs[r] = tp->out[r];
+  }
+  if (app) {
+    p.new_k = app->key;
+    p.new_v = app->value;
+    p.nk_token = app->k_token;
+    p.nk_head = app->k_head;
+    p.nv_token = app->v_token;
+    p.nv_head = app->v_head;
+    p.k_pool = L->k_cache;
+    p.v_pool = L->v_cache;
   }
   const int64_t rows = int64_t(L->num_blocks) * L->num_kv_heads * L->block_size;
   CUtensorMap tk, tv;
@@ -728,6 +744,38 @@ fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, void *out
                          workspace_bytes, stream);
   return launch_generic(layer, query, out, nullptr, context_lens, block_tables, max_blocks_per_seq,
                         num_seqs, num_heads, n_rep, num_seqs, scale, stream);
+}
+
+fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *query, const void *key,
+                                 const void *value, int64_t key_stride_token,
+                                 int64_t key_stride_head, int64_t value_stride_token,
+                                 int64_t value_stride_head, void *out, const int32_t *context_lens,
+                                 const int32_t *block_tables, int32_t max_blocks_per_seq,
+                                 int32_t num_seqs, int32_t num_heads, int32_t n_rep,
+                                 int32_t max_context_len, float scale, void *workspace,
+                                 size_t workspace_bytes, fa_stream_t stream) {
+  const char *who = "paged_decode_append";
+  if (fa_status s = check_attention_args(who, layer, query, out, context_lens, block_tables,
+                                         max_blocks_per_seq, num_seqs, num_heads, n_rep,
+                                         max_context_len, scale);
+      s != FA_OK)
+    return s;
+  if (!key || !value) return fail(FA_EINVAL, "%s: key/value is NULL", who);
+  if (key_stride_token < 0 || key_stride_head < 0 || value_stride_token < 0 || value_stride_head < 0)
+    return fail(FA_EINVAL, "%s: negative key/value stride", who);
+  if (num_seqs == 0) return ok();
+  if (max_context_len < 1) return fail(FA_ERANGE, "%s: max_context_len must be >= 1", who);
+  if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "%s: more than 65535 sequences per call", who);
+  if (!decode_fast_path(layer, n_rep, query, out))
+    return fail(FA_EUNSUPPORTED,
+                "%s: needs a 16-bit pool, block_size 16, head_dim 64/128, n_rep <= 8 and 16-byte "
+                "aligned buffers (use fa_reshape_and_cache + fa_paged_decode otherwise)", who);
+  const AppendArgs app{key, value, key_stride_token, key_stride_head, value_stride_token,
+                       value_stride_head};
+  return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq,
+                       num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                       workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr, true,
+                       &app);
 }
 
 fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *out,

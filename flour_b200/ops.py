@@ -138,6 +138,31 @@ def paged_decode(query, k_cache, v_cache, block_tables, context_lens, n_rep: int
     return out
 
 
+def paged_decode_append(query, k_cache, v_cache, key, value, block_tables, context_lens,
+                        n_rep: int, scale: float, max_context_len: int,
+                        workspace: Workspace | None = None, out=None, stream=None):
+    """Write each sequence's new token (key/value [B, kv_heads, d], any token/head strides,
+    unit stride on d) at position context_lens[b]-1, then decode query [B, Hq, d] over the whole
+    context, in one launch: reshape_and_cache + paged_decode of a decode step."""
+    layer = layer_desc(k_cache, v_cache)
+    query = query.contiguous()
+    if key.stride(-1) != 1 or value.stride(-1) != 1:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "key/value need unit stride on head_dim")
+    if key.dtype != k_cache.dtype or value.dtype != k_cache.dtype:
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, "key/value dtype differs from the pool dtype")
+    out = torch.empty_like(query) if out is None else out
+    bt, cl = _i32(block_tables, "block_tables"), _i32(context_lens, "context_lens")
+    B, hq, d = query.shape
+    need = workspace_size(B, hq, k_cache.shape[1], d, max_context_len, 1)
+    wp, wn = _ws_args(workspace, need)
+    check(lib().fa_paged_decode_append(ctypes.byref(layer), _ptr(query), _ptr(key), _ptr(value),
+                                       key.stride(0), key.stride(1), value.stride(0),
+                                       value.stride(1), _ptr(out), _ptr(cl), _ptr(bt),
+                                       bt.shape[1], B, hq, n_rep, max_context_len, scale, wp, wn,
+                                       _stream(stream)), "paged_decode_append")
+    return out
+
+
 def paged_decode_noalloc(query, k_cache, v_cache, block_tables, context_lens, n_rep: int,
                         scale: float, max_context_len: int, out=None, stream=None):
     """paged_decode without a workspace: the split-K scratch is the library's fixed buffer

@@ -171,6 +171,29 @@ FA_API fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, vo
                           int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
                           size_t workspace_bytes, fa_stream_t stream);
 
+/* One decode step of the reference's attention in one launch: Cache::write_kv of the new token
+ * (src/models/common/cache.rs:451 -> PagedKvPool::write, paged.rs:186-204) followed by
+ * paged_attention over the whole context (cpu.rs:57-112), the order of attention.rs:104-109.
+ * For each sequence b the new token is position L-1 of its context (L = context_lens[b] >= 1);
+ * key[b*key_stride_token + h*key_stride_head + x] (and value alike, strides in elements) is
+ * written to that position's slot, block_tables[b][(L-1)/16]*16 + (L-1)%16, for every KV head h,
+ * and query[b] then attends to positions 0..L-1, the new one included. Same result, bit for
+ * bit, as fa_reshape_and_cache with those slots followed by fa_paged_decode (same kernel, same
+ * split plan), minus one launch. The new token's slot must not lie inside another sequence's
+ * context in the same call (a shared prefix block is copied before it is written, as the
+ * reference's copy-on-write does). Sequences with an invalid length are not written (zero
+ * output, FA_DEVERR_CONTEXT). Requires the fast decode path (16-bit pool, block_size 16,
+ * head_dim 64/128, n_rep <= 8, 16-byte aligned query/out); other shapes: FA_EUNSUPPORTED. */
+FA_API fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *query,
+                                        const void *key, const void *value,
+                                        int64_t key_stride_token, int64_t key_stride_head,
+                                        int64_t value_stride_token, int64_t value_stride_head,
+                                        void *out, const int32_t *context_lens,
+                                        const int32_t *block_tables, int32_t max_blocks_per_seq,
+                                        int32_t num_seqs, int32_t num_heads, int32_t n_rep,
+                                        int32_t max_context_len, float scale, void *workspace,
+                                        size_t workspace_bytes, fa_stream_t stream);
+
 /* Decode without a caller-provided workspace. No counterpart in the reference: the reference's
  * CPU path never needs scratch memory. Some callers of this library cannot allocate device
  * memory at the point where they run attention — for example an engine whose KV pool was sized
