@@ -19,6 +19,8 @@
 // affected row is skipped.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "tcgen05.cuh"
 
 namespace fa {
@@ -338,8 +340,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // When the output has too few 128 x BN tiles to occupy the GPU (decode: 64 tokens), each tile is
 // computed by a cluster of S CTAs that split K. Each CTA accumulates its K slice in TMEM, copies
 // the f32 partial to its own shared memory, and signals every CTA of the cluster; CTA r then
-// sums rows [r*R, (r+1)*R) of all S partials through distributed shared memory and runs the
-// epilogue on them. No global workspace; the waits between CTAs are bounded mbarrier waits.
+// sums rows [r*R, (r+1)*R) of the tile's valid rows (R = ceil(valid / S)) over all S partials
+// through distributed shared memory, once, with plain loads the compiler can overlap, writes the
+// sums back over those rows of its own partial (no other CTA reads them there), and runs the
+// epilogue on them from local shared memory. No global workspace; the waits between CTAs are
+// bounded mbarrier waits.
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -396,26 +401,18 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t phase) 
 
 constexpr int kSplitMaxRanks = 8;
 
-// One row of the tile summed over the cluster's partials (f32 [128][BN + 4] in each CTA).
-struct SplitAcc {
-  uint32_t row_addr[kSplitMaxRanks];  // shared::cluster address of this row in each CTA
-  int nranks;
+// One row of the tile, already summed over the cluster's partials, in this CTA's shared memory.
+struct LocalAcc {
+  const float *row;
   __device__ __forceinline__ void ld32(int col, float (&v)[32]) const {
+    const float4 *p = reinterpret_cast<const float4 *>(row + col);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = 0.f;
-    for (int p = 0; p < nranks; ++p) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float x0, x1, x2, x3;
-        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(x0), "=f"(x1), "=f"(x2), "=f"(x3)
-                     : "r"(row_addr[p] + uint32_t(col + 4 * q) * 4u)
-                     : "memory");
-        v[4 * q] += x0;
-        v[4 * q + 1] += x1;
-        v[4 * q + 2] += x2;
-        v[4 * q + 3] += x3;
-      }
+    for (int q = 0; q < 8; ++q) {
+      const float4 x = p[q];
+      v[4 * q] = x.x;
+      v[4 * q + 1] = x.y;
+      v[4 * q + 2] = x.z;
+      v[4 * q + 3] = x.w;
     }
   }
 };
@@ -521,20 +518,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // Tell every CTA of the cluster (this one included) that this thread's row is in place.
     for (uint32_t p = 0; p < nranks; ++p) mbar_arrive_remote(map_to_rank(bar(PREADY), p));
     ok = mbar_wait_cluster(bar(PREADY), 0) && ok;
-    if (!ok) {
-      report(FA_DEVERR_TIMEOUT);
-    } else {
-      // Rows [rank*R, rank*R + R) of the tile: summed over all partials, then the epilogue.
-      const int R = (128 + int(nranks) - 1) / int(nranks);
-      const int t = tid - 64;  // 0..127 over the four epilogue warps
-      const int row = int(rank) * R + t;
-      if (t < R && row < 128) {
-        SplitAcc acc;
-        acc.nranks = int(nranks);
-        const uint32_t own_row = smem_u32(part + row * kPitch);
-        for (uint32_t p = 0; p < nranks; ++p) acc.row_addr[p] = map_to_rank(own_row, p);
-        epi.template operator()<BN>(acc, m * 128 + row, n * BN, s);
+    if (!ok) report(FA_DEVERR_TIMEOUT);
+    // Rows [rank*R, rank*R + R) of the tile's valid rows: summed over all partials into this
+    // CTA's own copy of those rows by all 128 epilogue threads (one float4 of one row each, the
+    // loads from every rank independent), then the epilogue reads them locally. Every epilogue
+    // thread reaches the named barrier, whatever its wait returned.
+    const int valid = min(128, s.M - m * 128);
+    const int R = (valid + int(nranks) - 1) / int(nranks);
+    const int t = tid - 64;  // 0..127 over the four epilogue warps
+    const int row0 = int(rank) * R;
+    const int rows = max(0, min(R, valid - row0));
+    if (ok) {
+      namespace cg = cooperative_groups;
+      cg::cluster_group cluster = cg::this_cluster();
+      const float4 *src[kSplitMaxRanks];
+#pragma unroll
+      for (int p = 0; p < kSplitMaxRanks; ++p)
+        src[p] = reinterpret_cast<const float4 *>(
+            cluster.map_shared_rank(part, uint32_t(p) < nranks ? uint32_t(p) : 0u));
+      float4 *own4 = reinterpret_cast<float4 *>(part);
+      constexpr int kUnits = BN / 4;  // float4 per row
+      for (int u = t; u < rows * kUnits; u += 128) {
+        const int idx = (row0 + u / kUnits) * (kPitch / 4) + u % kUnits;
+        float4 sum = src[0][idx];
+#pragma unroll
+        for (int p = 1; p < kSplitMaxRanks; ++p) {
+          if (uint32_t(p) >= nranks) break;
+          const float4 x = src[p][idx];
+          sum.x += x.x;
+          sum.y += x.y;
+          sum.z += x.z;
+          sum.w += x.w;
+        }
+        own4[idx] = sum;
       }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+    if (ok && t < rows) {
+      const int row = row0 + t;
+      epi.template operator()<BN>(LocalAcc{part + row * kPitch}, m * 128 + row, n * BN, s);
     }
   }
   tc::fence_before();
