@@ -20,8 +20,10 @@
 // ring in shared memory. K/V loads run ahead across item boundaries, and each Q tile is reloaded
 // as soon as the previous item's last MMA reading it has completed.
 //
-// Warp roles (320 threads): warps 0-3 softmax for tile A (thread = TMEM lane = Q row),
-// warps 4-7 softmax for tile B, warp 8 TMA producer + scheduler, warp 9 MMA issuer + TMEM owner.
+// Warp roles (576 threads): warps 0-7 softmax for tile A, warps 8-15 for tile B (warp = column
+// half x row quadrant: thread = TMEM lane = Q row, 64 of the row's 128 scores; the two warps of a
+// quadrant exchange row maxima through shared memory), warp 16 TMA producer + scheduler, warp 17
+// MMA issuer + TMEM owner.
 //
 // Memory: Q tiles and 2-stage K and V rings in shared memory, all 128-byte swizzled (K-major Q/K,
 // MN-major V). K/V tiles are 128 tokens = 8 pages gathered through the block table with one
