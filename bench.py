@@ -787,14 +787,41 @@ def run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, ba
 def run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_ranks, barrier):
     """Llama-3-8B layer projections through the fused kernels: QKV + RoPE + reshape_and_cache
     (hidden 4096 -> 48 heads x 128) and o_proj + residual (4096 -> 4096), at the C3 prefill
-    token count and at the C2 decode batch (64 tokens)."""
+    token count and at the C2 decode batch (64 tokens), plus the engine's logits readback at
+    the C2 batch: final RMSNorm + lm_head (128256 x 4096) on each sequence's last token, f32.
+    Each measurement replays a CUDA graph of `reps` calls that cycle through three copies of
+    the weights (more than L2 together), so weights stream from HBM and no host launch
+    overhead is timed."""
     from flour_b200.paged import rope_tables
-    hidden, Hq, Hkv, d = 4096, 32, 8, 128
+    hidden, Hq, Hkv, d, vocab = 4096, 32, 8, 128, 128256
     N = (Hq + 2 * Hkv) * d
     g = torch.Generator(device=dev).manual_seed(seed + 7)
-    w = (torch.randn(N, hidden, device=dev, generator=g) / 64).to(torch.bfloat16)
-    wo = (torch.randn(hidden, Hq * d, device=dev, generator=g) / 64).to(torch.bfloat16)
+    copies = 3
+    ws = [(torch.randn(N, hidden, device=dev, generator=g) / 64).to(torch.bfloat16)
+          for _ in range(copies)]
+    wos = [(torch.randn(hidden, Hq * d, device=dev, generator=g) / 64).to(torch.bfloat16)
+           for _ in range(copies)]
     cos, sin = rope_tables(d, 8192, 500000.0, torch.bfloat16, dev)
+
+    def timed(fns, reps):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for r in range(reps):
+                fns[r % len(fns)]()
+        graph.replay()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        return max_over_ranks(e0.elapsed_time(e1)) / reps
+
     res = {}
     for name, T in (("prefill_c3_tokens", 15401), ("decode_c2_batch", 64)):
         x = torch.randn(T, hidden, device=dev, generator=g).to(torch.bfloat16)
@@ -806,29 +833,43 @@ def run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_r
         slots = torch.arange(T, dtype=torch.int32, device=dev)
         q = torch.empty(T, Hq, d, device=dev, dtype=torch.bfloat16)
         out = torch.empty(T, hidden, device=dev, dtype=torch.bfloat16)
-        fns = {"qkv_rope_cache": lambda: ops.qkv_rope_cache(x, w, kc, vc, pos, slots, Hq, cos, sin,
-                                                            q_out=q),
-               "o_proj_residual": lambda: ops.o_proj_residual(a, wo, x, out=out)}
+        fns = {"qkv_rope_cache": [lambda w=w: ops.qkv_rope_cache(x, w, kc, vc, pos, slots, Hq, cos,
+                                                                 sin, q_out=q) for w in ws],
+               "o_proj_residual": [lambda wo=wo: ops.o_proj_residual(a, wo, x, out=out)
+                                   for wo in wos]}
         flops = {"qkv_rope_cache": 2 * T * hidden * N, "o_proj_residual": 2 * T * Hq * d * hidden}
         wbytes = {"qkv_rope_cache": N * hidden * 2, "o_proj_residual": hidden * Hq * d * 2}
         entry = {"tokens": T}
-        for k, fn in fns.items():
-            for _ in range(3):
-                fn()
-            torch.cuda.synchronize()
-            barrier()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = 20
-            e0.record(stream)
-            for _ in range(reps):
-                fn()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+        for k, fl in fns.items():
+            ms = timed(fl, 12 if T > 1024 else 60)
             entry[k] = {"ms": round(ms, 4), "tflops": round(flops[k] / ms / 1e9, 1),
                         "frac_of_measured_tensor_peak": round(flops[k] / ms / 1e9 / tc_peak, 4),
-                        "weight_gbps": round(wbytes[k] / ms / 1e6, 1)}
+                        "weight_gbps": round(wbytes[k] / ms / 1e6, 1),
+                        "weight_frac_of_measured_hbm_peak": round(wbytes[k] / ms / 1e6 / hbm_peak, 4)}
         res[name] = entry
+    del ws, wos
+    # Logits readback at the C2 batch: 64 sequences' last tokens through norm + lm_head.
+    B = 64
+    lm = (torch.randn(vocab, hidden, device=dev, generator=g) / 64).to(torch.bfloat16)
+    hid = torch.randn(B, hidden, device=dev, generator=g).to(torch.bfloat16)
+    nw = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    normed = torch.empty(B, hidden, device=dev, dtype=torch.bfloat16)
+    logits = torch.empty(B, vocab, device=dev, dtype=torch.float32)
+    ms = timed([lambda: ops.last_token_logits(hid, cu, lm, nw, 1e-5, normed_out=normed,
+                                              logits_out=logits)], 20)
+    host = torch.empty(B, vocab, dtype=torch.float32, pin_memory=True)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    host.copy_(logits, non_blocking=True)
+    r1.record(stream)
+    torch.cuda.synchronize()
+    lbytes = vocab * hidden * 2
+    res["logits_c2_batch"] = {"sequences": B, "vocab": vocab, "ms": round(ms, 4),
+                              "weight_gbps": round(lbytes / ms / 1e6, 1),
+                              "weight_frac_of_measured_hbm_peak": round(lbytes / ms / 1e6 / hbm_peak, 4),
+                              "readback_ms": round(r0.elapsed_time(r1), 4),
+                              "readback_bytes": B * vocab * 4}
     assert ops.device_status() == 0
     return res
 

@@ -109,6 +109,7 @@ SIGNATURES = {
                                 _F, _P, _SZ, _P]),
     "fa_qkv_rope_cache": (_I32, [_LP, _WP, _P, _P, _P, _I32, _P, _P]),
     "fa_o_proj_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P]),
+    "fa_last_token_logits": (_I32, [_P, _P, _I32, _I32, _P, _F, _P, _I32, _I32, _I32, _P, _P, _P]),
     "fa_ipc_alloc": (_I32, [_SZ, ctypes.POINTER(_P), _HP]),
     "fa_ipc_free": (_I32, [_P]),
     "fa_ipc_open": (_I32, [_HP, ctypes.POINTER(_P)]),

@@ -921,6 +921,48 @@ fa_status fa_o_proj_residual(const void *attn, const void *weight, const void *r
   return launch_gemm<__half>(num_tokens, out_features, in_features, epi, attn, weight, dtype, st, who);
 }
 
+fa_status fa_last_token_logits(const void *hidden, const int32_t *cu_seqlens, int32_t num_seqs,
+                               int32_t total_tokens, const void *norm_weight, float rms_eps,
+                               const void *lm_head, int32_t hidden_size, int32_t vocab,
+                               int32_t dtype, void *normed_out, float *logits_out,
+                               fa_stream_t stream) {
+  const char *who = "last_token_logits";
+  if (num_seqs < 0) return fail(FA_EINVAL, "%s: num_seqs %d < 0", who, num_seqs);
+  if (num_seqs == 0) return ok();
+  if (!hidden || !cu_seqlens || !lm_head || !normed_out || !logits_out)
+    return fail(FA_EINVAL, "%s: NULL hidden/cu_seqlens/lm_head/normed_out/logits_out", who);
+  if (dtype != FA_BF16 && dtype != FA_F16)
+    return fail(dtype == FA_F32 ? FA_EUNSUPPORTED : FA_EINVAL, "%s: dtype %d (bf16 or f16)", who, dtype);
+  if (total_tokens < 1) return fail(FA_EINVAL, "%s: total_tokens %d < 1", who, total_tokens);
+  if (hidden_size <= 0 || hidden_size % 8 != 0)
+    return fail(FA_EINVAL, "%s: hidden_size %d must be a positive multiple of 8", who, hidden_size);
+  if (vocab <= 0 || vocab % 32 != 0)
+    return fail(FA_EINVAL, "%s: vocab %d must be a positive multiple of 32", who, vocab);
+  if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "%s: more than 65535 sequences per call", who);
+  if (!(rms_eps >= 0.f) || !std::isfinite(rms_eps))
+    return fail(FA_EINVAL, "%s: rms_eps must be finite and >= 0", who);
+  if (!aligned(hidden, 16) || !aligned(lm_head, 16) || !aligned(normed_out, 16) ||
+      !aligned(logits_out, 16) || (norm_weight && !aligned(norm_weight, 2)))
+    return fail(FA_EINVAL, "%s: misaligned hidden/lm_head/normed_out/logits_out (16 B)", who);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == FA_BF16) {
+    using T = __nv_bfloat16;
+    fa::last_rows_norm_kernel<T><<<num_seqs, fa::kNormThreads, 0, st>>>(
+        static_cast<const T *>(hidden), cu_seqlens, total_tokens, static_cast<const T *>(norm_weight),
+        rms_eps, hidden_size, static_cast<T *>(normed_out));
+    if (fa_status s = check_launch(who); s != FA_OK) return s;
+    return launch_gemm<T>(num_seqs, vocab, hidden_size, fa::F32Epilogue{logits_out}, normed_out,
+                          lm_head, dtype, st, who);
+  }
+  using T = __half;
+  fa::last_rows_norm_kernel<T><<<num_seqs, fa::kNormThreads, 0, st>>>(
+      static_cast<const T *>(hidden), cu_seqlens, total_tokens, static_cast<const T *>(norm_weight),
+      rms_eps, hidden_size, static_cast<T *>(normed_out));
+  if (fa_status s = check_launch(who); s != FA_OK) return s;
+  return launch_gemm<T>(num_seqs, vocab, hidden_size, fa::F32Epilogue{logits_out}, normed_out,
+                        lm_head, dtype, st, who);
+}
+
 // ---- head-sharded decode ------------------------------------------------------------------
 
 static_assert(FA_MAX_TP == fa::kMaxTp, "FA_MAX_TP and the kernel's rank limit differ");

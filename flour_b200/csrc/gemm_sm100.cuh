@@ -223,6 +223,66 @@ struct ResidualEpilogue {
   }
 };
 
+// f32 output, no other work: the logits of the lm_head projection (read back as f32 by the
+// engine, engine.rs:221-222).
+struct F32Epilogue {
+  float *out;  // [M, N], N % 32 == 0, 16-byte aligned
+
+  template <int BN, class Acc>
+  __device__ void operator()(const Acc &acc, int row, int col0, const GemmShape &s) const {
+    const bool row_ok = row < s.M;
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = col0 + c * 32;  // warp-uniform
+      if (col >= s.N) break;
+      float v[32];
+      acc.ld32(c * 32, v);
+      if (!row_ok) continue;
+      float4 *d = reinterpret_cast<float4 *>(out + size_t(row) * s.N + col);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  }
+};
+
+// The final RMSNorm (CausalLM::forward, src/models/common/model.rs:56) of the last token of each
+// sequence of a packed batch: the only rows whose logits the engine reads (engine.rs:221). One
+// CTA per sequence; f32 math, one rounding to the model dtype (the GEMM operand). A sequence
+// whose token range is empty or outside the batch gets a zero row and FA_DEVERR_SEQLEN.
+constexpr int kNormThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    last_rows_norm_kernel(const T *hidden, const int32_t *cu_seqlens, int total_tokens,
+                          const T *weight, float eps, int H, T *out) {
+  __shared__ float s_red[kNormThreads / 32];
+  const int seq = blockIdx.x, tid = threadIdx.x;
+  const int a = cu_seqlens[seq], b = cu_seqlens[seq + 1];
+  T *o = out + size_t(seq) * H;
+  if (!(a >= 0 && b > a && b <= total_tokens)) {
+    if (tid == 0) report(FA_DEVERR_SEQLEN);
+    for (int i = tid; i < H; i += kNormThreads) o[i] = Elem<T>::from_f(0.f);
+    return;
+  }
+  const T *x = hidden + size_t(b - 1) * H;
+  float ss = 0.f;
+  for (int i = tid; i < H; i += kNormThreads) {
+    const float v = to_f32(x[i]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+  if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += s_red[w];
+  const float inv = rsqrtf(tot / float(H) + eps);
+  for (int i = tid; i < H; i += kNormThreads) {
+    const float wv = weight ? to_f32(weight[i]) : 1.f;
+    o[i] = Elem<T>::from_f(to_f32(x[i]) * inv * wv);
+  }
+}
+
 // ---- the persistent GEMM ---------------------------------------------------------------------
 
 template <typename T, int BN, class Epi>

@@ -284,6 +284,32 @@ def qkv_rope_cache(x, weight, k_cache, v_cache, positions, slot_mapping, num_hea
     return q_out
 
 
+def last_token_logits(hidden, cu_seqlens, lm_head, norm_weight=None, rms_eps: float = 1e-6,
+                      normed_out=None, logits_out=None, stream=None) -> torch.Tensor:
+    """f32 logits [S, vocab] of each sequence's last token: final RMSNorm + lm_head
+    (model.rs:56-58) on the rows the engine reads (engine.rs:220-222). hidden [T, H] packed,
+    cu_seqlens int32 [S + 1], lm_head [vocab, H]."""
+    dt = hidden.dtype
+    hidden = _c16(hidden, "hidden", dt)
+    lm_head = _c16(lm_head, "lm_head", dt)
+    _c16(norm_weight, "norm_weight", dt)
+    cu = _i32(cu_seqlens, "cu_seqlens")
+    T, H = hidden.shape
+    S = cu.numel() - 1
+    V = lm_head.shape[0]
+    if lm_head.shape[1] != H or (norm_weight is not None and tuple(norm_weight.shape) != (H,)):
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"lm_head must be [vocab, {H}] (norm_weight [{H}])")
+    if normed_out is None:
+        normed_out = torch.empty((S, H), dtype=dt, device=hidden.device)
+    if logits_out is None:
+        logits_out = torch.empty((S, V), dtype=torch.float32, device=hidden.device)
+    check(lib().fa_last_token_logits(_ptr(hidden), _ptr(cu), S, T, _ptr(norm_weight),
+                                     float(rms_eps), _ptr(lm_head), H, V, fa_dtype(dt),
+                                     _ptr(normed_out), _ptr(logits_out), _stream(stream)),
+          "last_token_logits")
+    return logits_out
+
+
 def o_proj_residual(attn, weight, residual=None, out=None, stream=None) -> torch.Tensor:
     """out = residual + attn @ weight^T (residual optional, may alias out).
 

@@ -269,6 +269,29 @@ FA_API fa_status fa_o_proj_residual(const void *attn, const void *weight, const 
                                     void *out, int32_t num_tokens, int32_t in_features,
                                     int32_t out_features, int32_t dtype, fa_stream_t stream);
 
+/* The logits the engine reads after a forward: the final RMSNorm (CausalLM::forward,
+ * src/models/common/model.rs:56) and lm_head (model.rs:58) applied to the last token of each
+ * sequence, as f32 (engine.rs:220-222 takes logits[seq_len-1] and converts it to f32). The
+ * reference projects every position and keeps the last; rows are independent, so only the
+ * last rows are computed.
+ *   hidden      [total_tokens, hidden_size] packed tokens (sequence s = rows
+ *               cu_seqlens[s] .. cu_seqlens[s+1]-1), 16-bit
+ *   norm_weight [hidden_size] or NULL (no scale), rms_eps its epsilon
+ *   lm_head     [vocab, hidden_size] (candle Linear layout; a tied embedding works the same)
+ *   normed_out  [num_seqs, hidden_size] scratch that receives the normalised last rows
+ *   logits_out  [num_seqs, vocab] f32, device; copy it to the host (pinned memory,
+ *               cudaMemcpyAsync on the same stream) for the sampler.
+ * The norm is computed in f32 and rounded once to the model dtype (the GEMM operand); the
+ * logits are accumulated in f32 and not rounded (the reference rounds them to the model dtype
+ * before converting to f32). Requires dtype FA_BF16 or FA_F16, hidden_size % 8 == 0,
+ * vocab % 32 == 0, 16-byte aligned hidden / lm_head / normed_out / logits_out. A sequence with
+ * an empty or out-of-range token range gets zero logits and FA_DEVERR_SEQLEN. */
+FA_API fa_status fa_last_token_logits(const void *hidden, const int32_t *cu_seqlens,
+                                      int32_t num_seqs, int32_t total_tokens,
+                                      const void *norm_weight, float rms_eps, const void *lm_head,
+                                      int32_t hidden_size, int32_t vocab, int32_t dtype,
+                                      void *normed_out, float *logits_out, fa_stream_t stream);
+
 /* ---- head-sharded decode (tensor parallel over KV heads, one process per GPU) ----------
  * The reference runs attention on one CPU and has no sharding (its plan shards sequences,
  * which needs no exchange). This optional mode splits a layer's KV heads over `tp` GPUs: rank r

@@ -10,6 +10,8 @@ DecoderLayer::forward (src/models/common/transformer.rs:37-38):
                       (src/models/common/cache.rs:378-392)                      attention.rs:96-99
 * ``qkv_forward``     the three above, per token, for packed tokens with their own positions
 * ``o_proj_residual`` residual + o_proj(attn)                                   attention.rs:116
+* ``final_logits``    CausalLM::forward's tail: final RMSNorm, lm_head, every row  model.rs:56-58
+* ``last_token_logits`` the row the engine reads per sequence, as f32          engine.rs:220-222
 
 candle-nn is not vendored (candle 0.9.2, Cargo.lock:233-236); ``rope`` restates the published
 rotate-half rotation that ``rotary_emb::rope`` implements: for i < d/2,
@@ -113,3 +115,22 @@ def o_proj_residual(attn, weight, residual=None, flow="f32", dtype="bf16"):
         if flow == "candle":
             y = round_to(y, dtype)
     return y
+
+
+def final_logits(hidden, norm_w, lm_head, eps, flow="f32", dtype="bf16", norm_flow=None):
+    """CausalLM::forward (model.rs:56-58): the final RMSNorm then lm_head, for every row.
+    ``norm_flow`` overrides the flow of the norm alone (the kernels round the norm to the model
+    dtype, as candle does, and keep the logits in f32)."""
+    hidden = np.asarray(hidden, np.float64)
+    w = np.ones(hidden.shape[-1]) if norm_w is None else norm_w
+    x = rms_norm(hidden, w, eps, norm_flow or flow, dtype)
+    return linear(x, lm_head, None, flow, dtype)
+
+
+def last_token_logits(hidden, cu_seqlens, norm_w, lm_head, eps, flow="f32", dtype="bf16",
+                      norm_flow=None):
+    """engine.rs:220-222: the logits of every position, then row seq_len - 1 of each sequence
+    (``logits.i((0, seq_len - 1))``), converted to f32."""
+    logits = final_logits(hidden, norm_w, lm_head, eps, flow, dtype, norm_flow)
+    last = np.asarray(cu_seqlens, np.int64)[1:] - 1
+    return logits[last]

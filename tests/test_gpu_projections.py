@@ -217,3 +217,61 @@ def test_fused_layer_matches_unfused_path(device):
     want = P.o_proj_residual(y, f64(wo), f64(c["x"]))
     got = f64(out)
     assert np.abs(got - want).max() <= 5e-2, np.abs(got - want).max()
+
+
+# ---- fa_last_token_logits: final RMSNorm + lm_head on each sequence's last token ------------
+
+def make_logits_case(device, lens, H, V, dtype, seed, norm=True):
+    g = torch.Generator().manual_seed(seed)
+    T = int(sum(lens))
+    hidden = (torch.randn((T, H), generator=g) * 2.0).to(dtype).to(device)
+    w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(dtype).to(device) if norm else None
+    lm = (torch.randn((V, H), generator=g) / math.sqrt(H)).to(dtype).to(device)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=device)
+    return hidden, w, lm, cu
+
+
+@pytest.mark.parametrize("lens,H,V,dtype", [
+    ([5, 1, 34, 1], 512, 1024, torch.bfloat16),
+    ([3] * 200, 256, 2048, torch.bfloat16),      # 200 sequences: two 128-row M tiles
+    ([64] * 8, 1024, 4096, torch.float16),
+])
+def test_last_token_logits_vs_oracle(device, lens, H, V, dtype):
+    hidden, w, lm, cu = make_logits_case(device, lens, H, V, dtype, seed=len(lens) + H)
+    logits = ops.last_token_logits(hidden, cu, lm, w, 1e-5)
+    # The engine's readback: f32 rows into pinned host memory on the same stream.
+    host = torch.empty(logits.shape, dtype=torch.float32, pin_memory=True)
+    host.copy_(logits, non_blocking=True)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    dt = "bf16" if dtype == torch.bfloat16 else "f16"
+    args = (f64(hidden), cu.cpu().numpy(), None if w is None else f64(w), f64(lm), 1e-5)
+    # Kernel flow: the norm rounded once to the model dtype (the GEMM operand), logits in f32.
+    close(host.numpy(), P.last_token_logits(*args, flow="f32", dtype=dt, norm_flow="candle"))
+    # The reference's own flow rounds the norm and the logits to the model dtype.
+    close(host.numpy(), P.last_token_logits(*args, flow="candle", dtype=dt), 3e-2, 2e-2)
+
+
+def test_last_token_logits_no_norm_weight_and_bad_sequence(device):
+    hidden, _, lm, cu = make_logits_case(device, [7, 9, 4], 256, 512, torch.bfloat16, 3, norm=False)
+    ops.device_status()
+    logits = ops.last_token_logits(hidden, cu, lm, None, 1e-6)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    close(f64(logits), P.last_token_logits(f64(hidden), cu.cpu().numpy(), None, f64(lm), 1e-6,
+                                           dtype="bf16", norm_flow="candle"))
+    bad = cu.clone()
+    bad[2] = bad[1]  # sequence 1 empty: zero logits and FA_DEVERR_SEQLEN, the others intact
+    logits2 = ops.last_token_logits(hidden, bad, lm, None, 1e-6)
+    torch.cuda.synchronize()
+    assert ops.device_status() & _lib.FA_DEVERR_SEQLEN
+    assert not logits2[1].any()
+    assert torch.equal(logits2[2], logits[2])
+
+
+def test_last_token_logits_rejects_bad_arguments(device):
+    hidden, w, lm, cu = make_logits_case(device, [4, 4], 256, 512, torch.bfloat16, 4)
+    with pytest.raises(_lib.FlourAttnError):
+        ops.last_token_logits(hidden, cu, lm[:500], w)        # vocab not a multiple of 32
+    with pytest.raises(_lib.FlourAttnError):
+        ops.last_token_logits(hidden.float(), cu, lm, w)      # f32 hidden

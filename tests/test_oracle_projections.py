@@ -78,3 +78,25 @@ def test_o_proj_residual_oracle():
     a, w, res = rng.standard_normal((5, 32)), rng.standard_normal((16, 32)), rng.standard_normal((5, 16))
     assert np.allclose(P.o_proj_residual(a, w, res), res + a @ w.T)
     assert np.allclose(P.o_proj_residual(a, w), a @ w.T)
+
+
+def test_last_token_logits_oracle():
+    # engine.rs:220-222 reads row seq_len-1 of logits computed for every position; the oracle's
+    # last_token_logits must equal that row of the full final_logits, per packed sequence, and
+    # the norm must be a plain RMSNorm (unit rows stay unit-RMS before the weight).
+    rng = np.random.default_rng(5)
+    T, H, V = 23, 64, 96
+    hidden = P.round_to(rng.standard_normal((T, H)) * 3.0, "bf16")
+    w = P.round_to(1.0 + 0.1 * rng.standard_normal(H), "bf16")
+    lm = P.round_to(rng.standard_normal((V, H)) / 8.0, "bf16")
+    cu = np.array([0, 1, 9, 10, 23])
+    full = P.final_logits(hidden, w, lm, 1e-6)
+    last = P.last_token_logits(hidden, cu, w, lm, 1e-6)
+    assert last.shape == (4, V)
+    assert np.array_equal(last, full[[0, 8, 9, 22]])
+    x = hidden[22]
+    ref = (x / np.sqrt(np.mean(x * x) + 1e-6) * w) @ lm.T
+    assert np.allclose(last[3], ref, rtol=1e-12, atol=1e-12)
+    # The candle flow (norm and logits rounded to bf16) stays within bf16 rounding of f32.
+    cand = P.last_token_logits(hidden, cu, w, lm, 1e-6, flow="candle")
+    assert np.abs(cand - last).max() <= 2e-2 + 1e-2 * np.abs(last).max()
