@@ -175,6 +175,77 @@ def time_oracle(arrays, threads: int, reps: int, budget_s: float):
     return times
 
 
+def cpu_config_baselines(seed: int, threads: int, budget_s: float = 4.0) -> dict:
+    """The CPU restatement of the reference path (cpu.rs:57-112) timed on bounded samples of
+    the other configurations, in each one's own unit: C1 whole (its 4 sequences, f32), C3 one
+    group of 4 sequences sharing a prefix (causal suffix FLOPs), C4 one 16K-32K sequence."""
+    import torch
+    import oracle
+    from flour_b200.workloads import LLAMA8B, c4_contexts, make_c1, make_c3, make_decode, to_numpy
+
+    def run(b, cu, n_rep, d, dt):
+        arr = (to_numpy(b.q), to_numpy(b.k_caches[0]), to_numpy(b.v_caches[0]), cu,
+               np.asarray(to_numpy(b.context_lens) if hasattr(b, "cu_seqlens_q") else b.ctx_host,
+                          np.int32), to_numpy(b.block_tables))
+        times, t_start = [], time.perf_counter()
+        while True:
+            t0 = time.perf_counter()
+            oracle.paged_attention(*arr, n_rep, 1 / math.sqrt(d), dtype=dt, threads=threads)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s or len(times) >= 200:
+                return statistics.median(times), len(times)
+
+    res = {}
+    b = make_c1("cpu", seed=1)
+    s, n = run(b, np.arange(b.num_seqs + 1, dtype=np.int32), 7, 64, oracle.DT_F32)
+    res["C1"] = {"value": round((b.kv_bytes_per_layer() + b.io_bytes_per_layer()) / s / 1e9, 3),
+                 "unit": "GB/s", "sample": f"C1 whole ({b.num_seqs} sequences, f32), {n} runs"}
+    p = make_c3("cpu", seed=seed + 3, num_seqs=4)
+    s, n = run(p, to_numpy(p.cu_seqlens_q), 4, 128, oracle.DT_BF16)
+    res["C3"] = {"value": round(p.flops() / s / 1e12, 5), "unit": "TFLOP/s",
+                 "sample": f"one C3 group: 4 sequences sharing a prefix, {int(p.lens.sum())} tokens, "
+                           f"{int((p.lens - p.prefix).sum())} new, {n} runs"}
+    ctx = c4_contexts(seed, 1)
+    d4 = make_decode(LLAMA8B, ctx, torch.bfloat16, "cpu", seed)
+    s, n = run(d4, np.arange(2, dtype=np.int32), 4, 128, oracle.DT_BF16)
+    res["C4"] = {"value": round(d4.kv_bytes_per_layer() / s / 1e9, 3), "unit": "GB/s",
+                 "sample": f"one C4 sequence of {int(ctx[0])} tokens, {n} runs"}
+    for v in res.values():
+        v["cores"] = threads
+        v["kind"] = "port"
+    return res
+
+
+def run_c1(torch, ops, dev, stream):
+    """C1 (the reference's CPU-runnable case: Qwen2.5-0.5B heads, f32, 4 sequences): one decode
+    launch, too small to load the GPU; reported for completeness (graph of 50 launches)."""
+    from flour_b200.workloads import make_c1
+    b = make_c1(dev, seed=1)
+    ws = ops.Workspace(dev)
+    out = torch.empty_like(b.q)
+    scale = 1.0 / math.sqrt(b.heads.head_dim)
+    call = lambda: ops.paged_decode(b.q, b.k_caches[0], b.v_caches[0], b.block_tables,
+                                    b.context_lens, b.heads.n_rep, scale, b.max_context_len, ws,
+                                    out=out)
+    call()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(50):
+            call()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / 50
+    nbytes = b.kv_bytes_per_layer() + b.io_bytes_per_layer()
+    return {"config": "C1: Qwen2.5-0.5B heads (14/2, d=64), f32, 4 sequences, ctx ~ U[33, 512]",
+            "us_per_launch": round(us, 2), "gbps": round(nbytes / us / 1e3, 2), "bytes": int(nbytes)}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -388,8 +459,11 @@ def run_ours(args):
         proj = run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_ranks,
                                barrier)
 
+    c1 = run_c1(torch, ops, dev, stream) if world == 1 else None
+
     # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------------
     cpu = None
+    cpu_cfg = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         import oracle
         threads = oracle.cpu_threads()
@@ -400,6 +474,7 @@ def run_ours(args):
                "cores": threads, "kind": "port",
                "sample": f"{len(times)} x one C2 layer of 16 sequences ({nbytes / 1e6:.0f} MB KV), "
                          "oracle restatement of src/backend/cpu.rs:57-112"}
+        cpu_cfg = cpu_config_baselines(args.seed, threads)
 
     clk = clocks.summary()
     if rank == 0:
@@ -435,6 +510,17 @@ def run_ours(args):
             line["projections"] = proj
         if c5:
             line["c5"] = c5
+        if c1:
+            line["c1"] = c1
+        if cpu_cfg:
+            gpu_vals = {"C1": c1["gbps"] if c1 else None,
+                        "C3": prefill["kernel_tflops"] if prefill else None,
+                        "C4": longctx["gbps"] if longctx else None}
+            for k, v in cpu_cfg.items():
+                if gpu_vals.get(k):
+                    v["gpu_value"] = gpu_vals[k]
+                    v["gpu_over_cpu"] = round(gpu_vals[k] / v["value"], 1)
+            line["cpu_baseline_configs"] = cpu_cfg
         if tp:
             line["tp_decode"] = tp
         print(json.dumps(line), flush=True)

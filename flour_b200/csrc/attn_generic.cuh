@@ -1,5 +1,6 @@
 // Generic paged attention: any element type, any head_dim <= 256, any block_size <= 1024,
-// any n_rep, any number of query tokens per sequence. One CTA per (query token, query head).
+// any n_rep, any number of query tokens per sequence. One CTA of 8 warps per (query token,
+// query head); the warps fold interleaved blocks and merge their states at the end.
 //
 // This is the per-row form of backend::cpu::paged_attention (src/backend/cpu.rs:57-112): the
 // sequence's KV is walked block by block in logical order (KvCache::gather_blocks,
@@ -33,17 +34,33 @@ struct GenericParams {
   float scale;
 };
 
-constexpr int kGenericThreads = 128;
+constexpr int kGenericWarps = 8;
+constexpr int kGenericThreads = kGenericWarps * 32;
 constexpr int kGenericMaxDim = 256;
 
+// Shared memory: q [kGenericMaxDim] | per-warp probabilities [kGenericWarps][block_size] |
+// per-warp partial accumulators [kGenericWarps][kGenericMaxDim] | per-warp max and sum.
+__host__ __device__ constexpr size_t generic_smem_floats(int block_size) {
+  return size_t(kGenericMaxDim) + size_t(kGenericWarps) * block_size +
+         size_t(kGenericWarps) * kGenericMaxDim + 2 * kGenericWarps;
+}
+
+// Each warp folds its own blocks (b = warp, warp + 8, ...) with the reference's block-wise
+// online softmax (scores of the block, block max, one correction, p = exp(s - max), sum, then
+// acc = acc * corr + sum_j p_j v_j), lanes over the block's rows for the scores and over
+// head_dim for the accumulation; the 8 partial states are merged at the end. Only blocks up to
+// the last visible position are folded, so every folded block holds at least one visible key.
 template <typename T>
 __global__ void __launch_bounds__(kGenericThreads) generic_attn_kernel(const GenericParams p) {
   extern __shared__ float gsm[];
-  float *qs = gsm;                    // [head_dim]
-  float *sc = gsm + kGenericMaxDim;   // [block_size]
-  const int qi = blockIdx.x, h = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int D = p.head_dim, BS = p.block_size;
+  float *qs = gsm;                                        // [D]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float *pw = gsm + kGenericMaxDim + size_t(warp) * BS;   // this warp's probabilities [BS]
+  float *accs = gsm + kGenericMaxDim + size_t(kGenericWarps) * BS;  // [W][kGenericMaxDim]
+  float *ms = accs + kGenericWarps * kGenericMaxDim;      // [W]
+  float *ls = ms + kGenericWarps;                         // [W]
+  const int qi = blockIdx.x, h = blockIdx.y;
   const size_t orow = (size_t(qi) * p.num_heads + h) * D;
   T *out = static_cast<T *>(p.out);
 
@@ -72,7 +89,8 @@ __global__ void __launch_bounds__(kGenericThreads) generic_attn_kernel(const Gen
     for (int x = tid; x < D; x += kGenericThreads) out[orow + x] = Elem<T>::from_f(0.f);
     return;
   }
-  const int offset = L - sq;  // cpu.rs:68
+  const int offset = L - sq;     // cpu.rs:68
+  const int limit = offset + i;  // this query sees keys j <= limit (cpu.rs:87-94)
   const int kh = h / p.n_rep;
   const T *qp = static_cast<const T *>(p.q) + orow;
   for (int x = tid; x < D; x += kGenericThreads) qs[x] = Elem<T>::to_f(qp[x]);
@@ -80,50 +98,81 @@ __global__ void __launch_bounds__(kGenericThreads) generic_attn_kernel(const Gen
 
   const T *kc = static_cast<const T *>(p.k_cache);
   const T *vc = static_cast<const T *>(p.v_cache);
-  float acc0 = 0.f, acc1 = 0.f;  // dims tid and tid + 128
+  constexpr int kPerLane = kGenericMaxDim / 32;
+  float acc[kPerLane];
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k) acc[k] = 0.f;
   float m = neg_inf(), l = 0.f;
-  const int nb = (L + BS - 1) / BS;
+  const int nb = limit / BS + 1;  // blocks holding a visible key
   const int32_t *table = p.block_tables + size_t(s) * p.max_blocks_per_seq;
   bool bad_id = false;
-  for (int b = 0; b < nb; ++b) {
+  for (int b = warp; b < nb; b += kGenericWarps) {
     int id = table[b];
     if (uint32_t(id) >= uint32_t(p.num_blocks)) { bad_id = true; id = 0; }
     const int kv_start = b * BS;
     const int bn = min(BS, L - kv_start);
     const size_t base = (size_t(id) * p.num_kv_heads + kh) * BS * size_t(D);
-    // Scores of this block (cpu.rs:84-94): one warp per key row, lanes over head_dim.
-    for (int j = warp; j < bn; j += kGenericThreads / 32) {
+    // Scores of this block (cpu.rs:84-94): lane r takes rows r, r + 32, ...
+    float bmax = neg_inf();
+    for (int j = lane; j < bn; j += 32) {
       const T *kr = kc + base + size_t(j) * D;
       float dot = 0.f;
-      for (int x = lane; x < D; x += 32) dot += qs[x] * Elem<T>::to_f(kr[x]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      if (lane == 0) sc[j] = (kv_start + j > offset + i) ? neg_inf() : dot * p.scale;
+      for (int x = 0; x < D; ++x) dot = fmaf(qs[x], Elem<T>::to_f(kr[x]), dot);
+      const float sc = (kv_start + j > limit) ? neg_inf() : dot * p.scale;
+      pw[j] = sc;
+      bmax = fmaxf(bmax, sc);
     }
-    __syncthreads();
-    // Fold (cpu.rs:96-105); every thread evaluates the same scalar recurrence.
-    float bmax = neg_inf();
-    for (int j = 0; j < bn; ++j) bmax = fmaxf(bmax, sc[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+    // Fold (cpu.rs:96-105): bmax is finite (row kv_start <= limit is visible).
     const float new_max = fmaxf(m, bmax);
     const float corr = expf(m - new_max);
-    float psum = 0.f, a0 = 0.f, a1 = 0.f;
-    for (int j = 0; j < bn; ++j) {
-      const float pj = expf(sc[j] - new_max);
+    float psum = 0.f;
+    for (int j = lane; j < bn; j += 32) {
+      const float pj = expf(pw[j] - new_max);
+      pw[j] = pj;
       psum += pj;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) acc[k] *= corr;
+    for (int j = 0; j < bn; ++j) {
+      const float pj = pw[j];
       const T *vr = vc + base + size_t(j) * D;
-      if (tid < D) a0 += pj * Elem<T>::to_f(vr[tid]);
-      if (tid + kGenericThreads < D) a1 += pj * Elem<T>::to_f(vr[tid + kGenericThreads]);
+#pragma unroll
+      for (int k = 0; k < kPerLane; ++k)
+        if (lane + 32 * k < D) acc[k] = fmaf(pj, Elem<T>::to_f(vr[lane + 32 * k]), acc[k]);
     }
     l = l * corr + psum;
-    acc0 = acc0 * corr + a0;
-    acc1 = acc1 * corr + a1;
     m = new_max;
-    __syncthreads();
+    __syncwarp();
   }
-  if (bad_id && tid == 0) report(FA_DEVERR_BLOCK_ID);
-  // cpu.rs:111: acc / running_sum, cast to the query dtype.
-  if (tid < D) out[orow + tid] = Elem<T>::from_f(acc0 / l);
-  if (tid + kGenericThreads < D) out[orow + tid + kGenericThreads] = Elem<T>::from_f(acc1 / l);
+  if (bad_id) report(FA_DEVERR_BLOCK_ID);
+  // Merge the warps' states; warps without blocks hold m = -inf and contribute nothing.
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k)
+    if (lane + 32 * k < D) accs[warp * kGenericMaxDim + lane + 32 * k] = acc[k];
+  if (lane == 0) {
+    ms[warp] = m;
+    ls[warp] = l;
+  }
+  __syncthreads();
+  float M = neg_inf();
+#pragma unroll
+  for (int w = 0; w < kGenericWarps; ++w) M = fmaxf(M, ms[w]);
+  float wsum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kGenericWarps; ++w)
+    if (ms[w] != neg_inf()) wsum += expf(ms[w] - M) * ls[w];
+  for (int x = tid; x < D; x += kGenericThreads) {
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGenericWarps; ++w)
+      if (ms[w] != neg_inf()) o += expf(ms[w] - M) * accs[w * kGenericMaxDim + x];
+    out[orow + x] = Elem<T>::from_f(o / wsum);  // cpu.rs:111: acc / running_sum, cast to q's dtype
+  }
 }
 
 }  // namespace fa

@@ -298,14 +298,21 @@ fa_status launch_generic(const fa_kv_layer *L, const void *q, void *out, const i
   p.num_blocks = L->num_blocks;
   p.total_q = total_q;
   p.scale = scale;
-  const size_t smem = (fa::kGenericMaxDim + L->block_size) * sizeof(float);
+  const size_t smem = fa::generic_smem_floats(L->block_size) * sizeof(float);
   dim3 grid(total_q, num_heads);
+  auto launch = [&](auto kern) -> fa_status {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess)
+      return fail(FA_ECUDA, "paged_attention (generic): set smem attribute: %s", cudaGetErrorString(e));
+    kern<<<grid, fa::kGenericThreads, smem, stream>>>(p);
+    return check_launch("paged_attention (generic)");
+  };
   switch (L->dtype) {
-    case FA_F32: fa::generic_attn_kernel<float><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
-    case FA_BF16: fa::generic_attn_kernel<__nv_bfloat16><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
-    default: fa::generic_attn_kernel<__half><<<grid, fa::kGenericThreads, smem, stream>>>(p); break;
+    case FA_F32: return launch(fa::generic_attn_kernel<float>);
+    case FA_BF16: return launch(fa::generic_attn_kernel<__nv_bfloat16>);
+    default: return launch(fa::generic_attn_kernel<__half>);
   }
-  return check_launch("paged_attention (generic)");
 }
 
 bool prefill_fast_path(const fa_kv_layer *L, int n_rep, int total_q, float scale, const void *q,
