@@ -178,10 +178,12 @@ def time_oracle(arrays, threads: int, reps: int, budget_s: float):
 def cpu_config_baselines(seed: int, threads: int, budget_s: float = 4.0) -> dict:
     """The CPU restatement of the reference path (cpu.rs:57-112) timed on bounded samples of
     the other configurations, in each one's own unit: C1 whole (its 4 sequences, f32), C3 one
-    group of 4 sequences sharing a prefix (causal suffix FLOPs), C4 one 16K-32K sequence."""
+    group of 4 sequences sharing a prefix (causal suffix FLOPs), C4 one 16K-32K sequence, C5 32 of
+    its decode sequences plus one of its prefills (tokens per second through its 28 layers)."""
     import torch
     import oracle
-    from flour_b200.workloads import LLAMA8B, c4_contexts, make_c1, make_c3, make_decode, to_numpy
+    from flour_b200.workloads import (LLAMA8B, QWEN7B, c4_contexts, c5_plan, make_c1, make_c3,
+                                      make_decode, make_prefill, to_numpy)
 
     def run(b, cu, n_rep, d, dt):
         arr = (to_numpy(b.q), to_numpy(b.k_caches[0]), to_numpy(b.v_caches[0]), cu,
@@ -210,6 +212,17 @@ def cpu_config_baselines(seed: int, threads: int, budget_s: float = 4.0) -> dict
     s, n = run(d4, np.arange(2, dtype=np.int32), 4, 128, oracle.DT_BF16)
     res["C4"] = {"value": round(d4.kv_bytes_per_layer() / s / 1e9, 3), "unit": "GB/s",
                  "sample": f"one C4 sequence of {int(ctx[0])} tokens, {n} runs"}
+    ctx5, is_pf, pf_len, _ = c5_plan(seed)
+    dec = np.nonzero(~is_pf)[0][:32]
+    pf = np.nonzero(is_pf)[0][:1]
+    db = make_decode(QWEN7B, ctx5[dec], torch.bfloat16, "cpu", seed)
+    pb = make_prefill(QWEN7B, pf_len[pf], np.zeros(1, np.int64), torch.bfloat16, "cpu", seed + 1)
+    t_dec, n1 = run(db, np.arange(len(dec) + 1, dtype=np.int32), 7, 128, oracle.DT_BF16)
+    t_pf, n2 = run(pb, to_numpy(pb.cu_seqlens_q), 7, 128, oracle.DT_BF16)
+    tokens = len(dec) + int(pf_len[pf].sum())
+    res["C5"] = {"value": round(tokens / ((t_dec + t_pf) * 28), 1), "unit": "tokens/s",
+                 "sample": f"{len(dec)} C5 decode sequences + one {int(pf_len[pf].sum())}-token "
+                           f"prefill, one layer timed ({n1}/{n2} runs), x28 layers"}
     for v in res.values():
         v["cores"] = threads
         v["kind"] = "port"
@@ -515,7 +528,8 @@ def run_ours(args):
         if cpu_cfg:
             gpu_vals = {"C1": c1["gbps"] if c1 else None,
                         "C3": prefill["kernel_tflops"] if prefill else None,
-                        "C4": longctx["gbps"] if longctx else None}
+                        "C4": longctx["gbps"] if longctx else None,
+                        "C5": c5["tokens_per_s"] if c5 else None}
             for k, v in cpu_cfg.items():
                 if gpu_vals.get(k):
                     v["gpu_value"] = gpu_vals[k]
