@@ -727,8 +727,9 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
     (ctx ~ LogNormal(ln 1024, 0.8) capped at 8192); about 10 % are new prompts of L ~ U[256, 2048]
     run as prefill, the rest decode one token. The sequences are partitioned longest-first over
     the ranks, so the total work is fixed as N grows (strong scaling). One step = per layer:
-    the decode sequences' new K/V write + decode (one fa_paged_decode_append launch), the
-    prefill sequences' reshape_and_cache and the prefill launch; each rank owns its
+    the decode sequences' new K/V write + decode (one fa_paged_decode_append launch) on one
+    stream, the prefill sequences' reshape_and_cache and the prefill launch on a second stream
+    (the two sub-batches share no data); each rank owns its
     own pools. KV values are zero-filled (timing only; the kernels' arithmetic does not depend on
     the values)."""
     from flour_b200.workloads import QWEN7B, c5_plan, lpt_partition, make_decode, make_prefill
@@ -753,38 +754,58 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
     ws_d, ws_p = ops.Workspace(dev), ops.Workspace(dev)
     ws_d.get(ops.workspace_size(B, h.num_heads, h.num_kv_heads, h.head_dim, db.max_context_len, 1))
 
+    # The decode sequences and the new prompts are independent through every layer, so they run
+    # as two streams (fork and join inside the step): decode CTAs fill the SMs the persistent
+    # prefill kernel leaves idle in its tail, and the other way round.
+    side = torch.cuda.Stream(device=dev)
+
     def step():
+        main = torch.cuda.current_stream()
+        side.wait_stream(main)
         for l in range(L):
             ops.paged_decode_append(dq, db.k_caches[l], db.v_caches[l], dk, dv, db.block_tables,
                                     db.context_lens, h.n_rep, scale, db.max_context_len, ws_d,
                                     out=dout)
-            if pb is not None:
-                ops.reshape_and_cache(pb.k_caches[l], pb.v_caches[l], pb.key, pb.value,
-                                      pb.slot_mapping)
-                ops.paged_prefill(pb.q, pb.k_caches[l], pb.v_caches[l], pb.cu_seqlens_q,
-                                  pb.context_lens, pb.block_tables, h.n_rep, scale,
-                                  pb.max_seqlen_q, pb.max_context_len, ws_p, out=pout)
+        if pb is not None:
+            with torch.cuda.stream(side):
+                for l in range(L):
+                    ops.reshape_and_cache(pb.k_caches[l], pb.v_caches[l], pb.key, pb.value,
+                                          pb.slot_mapping)
+                    ops.paged_prefill(pb.q, pb.k_caches[l], pb.v_caches[l], pb.cu_seqlens_q,
+                                      pb.context_lens, pb.block_tables, h.n_rep, scale,
+                                      pb.max_seqlen_q, pb.max_context_len, ws_p, out=pout)
+        main.wait_stream(side)
 
     for _ in range(2):
         step()
     torch.cuda.synchronize()
     assert ops.device_status() == 0
+    # The step as one CUDA graph (84 launches): the host's launch cost stays out of the timing.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
     barrier()
     reps = 5
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(reps):
-        step()
+        graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+    del graph
+    assert ops.device_status() == 0
+    own_ms = e0.elapsed_time(e1) / reps
+    ms = max_over_ranks(own_ms)
+    fastest_ms = -max_over_ranks(-own_ms)
     kvb = h.num_kv_heads * h.head_dim * 2 * 2
     dec_bytes = float(ctx[~is_pf].sum()) * kvb * L
     pf_flops = float((4.0 * h.num_heads * h.head_dim * pf_len[is_pf] * (pf_len[is_pf] + 1) / 2).sum()) * L
     tokens = int((~is_pf).sum() + pf_len[is_pf].sum())
     res = {"config": "C5 mixed serving step: Qwen2-7B heads, 28 layers, 512 seqs (ctx ~ LogNormal"
                      "(ln 1024, 0.8) <= 8192), ~10 % new prefills L ~ U[256, 2048]; LPT over ranks",
-           "scaling": "strong", "step_ms": round(ms, 4),
+           "scaling": "strong", "step_ms": round(ms, 4), "fastest_rank_step_ms": round(fastest_ms, 4),
            "tokens_per_s": round(tokens / (ms / 1e3), 1),
            "decode_seqs": int((~is_pf).sum()), "prefill_seqs": int(is_pf.sum()),
            "prefill_tokens": int(pf_len[is_pf].sum()),
