@@ -136,3 +136,29 @@ def test_bad_block_id_reported(device):
     ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens, bt, 4,
                       1 / math.sqrt(128), b.max_seqlen_q, b.max_context_len, ops.Workspace(device))
     assert ops.device_status() & _lib.FA_DEVERR_BLOCK_ID
+
+
+@pytest.mark.parametrize("heads", [LLAMA8B, QWEN7B])
+def test_prefix_reuse_leaves_suffix_rows_unchanged(device, heads):
+    # The invariance the reference checks end to end (model.rs:244-360, 1e-4 in f32): a prompt
+    # prefilled cold, and the same prompt prefilled as a suffix over its cached prefix, give the
+    # suffix tokens the same attention output. Here on the tcgen05 path (bf16): both runs read
+    # the same pool, so the outputs differ only by tile alignment (chunks start at different
+    # tokens), far inside the bf16 tolerance.
+    lens, P = [1000, 333], [512, 208]
+    cold = build(device, heads, lens, [0, 0], seed=77)
+    out_cold = run_and_check(cold)
+    # Same pool, tables and Q/K/V; only the last len - P tokens are queries.
+    h = heads
+    scale = 1 / math.sqrt(h.head_dim)
+    cu_cold = cold.cu_seqlens_q.cpu().numpy()
+    rows = np.concatenate([np.arange(cu_cold[i] + P[i], cu_cold[i + 1]) for i in range(len(lens))])
+    suffix = np.array(lens) - np.array(P)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(suffix)]), dtype=torch.int32, device=device)
+    q = cold.q[torch.from_numpy(rows).to(device)].contiguous()
+    out_warm = ops.paged_prefill(q, cold.k_caches[0], cold.v_caches[0], cu, cold.context_lens,
+                                 cold.block_tables, h.n_rep, scale, int(suffix.max()),
+                                 cold.max_context_len, ops.Workspace(device))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert max_abs(f32(out_warm), f32(out_cold)[rows]) <= 1e-2
