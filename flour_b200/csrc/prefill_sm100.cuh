@@ -320,25 +320,48 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       };
       int g = 0, v = 0;
       bool ok = true;
+      // S_X(0) of item `itm` (first KV tile g0, Q-tile phase v0).
+      auto start_tile = [&](int X, const PfItem &itm, int g0, int v0) -> bool {
+        const int st0 = g0 % kPfStages;
+        if (X == 0) {
+          if (!(mbar_wait(bar(S::QFULL + 0), v0 & 1) &&
+                mbar_wait(bar(S::KFULL + st0), (g0 / kPfStages) & 1)))
+            return false;
+          tc::fence_after();
+          issue_s(0, st0);
+          tc::commit(bar(S::SFULL + 0));
+          if (itm.n_tiles == 1) tc::commit(bar(S::QEMPTY + 0));
+        } else {
+          if (!mbar_wait(bar(S::QFULL + 1), v0 & 1)) return false;
+          tc::fence_after();
+          issue_s(1, st0);
+          tc::commit(bar(S::SFULL + 1));
+          tc::commit(bar(S::KEMPTY + st0));
+          if (itm.n_tiles == 1) tc::commit(bar(S::QEMPTY + 1));
+        }
+        return true;
+      };
+      // The next item is fetched during this item's last tile, and its S_A(0) / S_B(0) follow
+      // this item's last PV_A / PV_B at once: each Q tile's softmax warps find their next S ready
+      // when they finish this item's epilogue, instead of waiting for the other tile.
+      bool have_next = false, next_started = false;
+      PfItem next{};
       for (int k = 0; ok; ++k) {
         const int slot = k & 1;
-        if (!(ok = mbar_wait(bar(S::IFULL + slot), (k >> 1) & 1))) break;
-        const PfItem it = items[slot];
+        PfItem it;
+        bool started = false;
+        if (have_next) {
+          it = next;
+          started = next_started;
+          have_next = false;
+        } else {
+          if (!(ok = mbar_wait(bar(S::IFULL + slot), (k >> 1) & 1))) break;
+          it = items[slot];
+        }
         if (it.kind == 2) break;
         if (it.kind == 0) {
           const int n = it.n_tiles;
-          if (!(ok = mbar_wait(bar(S::QFULL + 0), v & 1) &&
-                     mbar_wait(bar(S::KFULL + g % kPfStages), (g / kPfStages) & 1))) break;
-          tc::fence_after();
-          issue_s(0, g % kPfStages);
-          tc::commit(bar(S::SFULL + 0));
-          if (n == 1) tc::commit(bar(S::QEMPTY + 0));
-          if (!(ok = mbar_wait(bar(S::QFULL + 1), v & 1))) break;
-          tc::fence_after();
-          issue_s(1, g % kPfStages);
-          tc::commit(bar(S::SFULL + 1));
-          tc::commit(bar(S::KEMPTY + g % kPfStages));
-          if (n == 1) tc::commit(bar(S::QEMPTY + 1));
+          if (!started && !(ok = start_tile(0, it, g, v) && start_tile(1, it, g, v))) break;
           for (int i = 0; ok && i < n; ++i) {
             const int gi = g + i;
             const int st = gi % kPfStages, st1 = (gi + 1) % kPfStages;
@@ -347,8 +370,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             if (!(ok = mbar_wait(bar(S::PFULL + 0), gi & 1) && mbar_wait(bar(S::VFULL + st), ph))) break;
             tc::fence_after();
             issue_pv(0, st, i == 0);
-            if (last) tc::commit(bar(S::ODONE + 0));
-            if (!last) {
+            if (last) {
+              tc::commit(bar(S::ODONE + 0));
+              if (!(ok = mbar_wait(bar(S::IFULL + (slot ^ 1)), ((k + 1) >> 1) & 1))) break;
+              next = items[slot ^ 1];
+              have_next = true;
+              next_started = false;
+              if (next.kind == 0 && !(ok = start_tile(0, next, g + n, v + 1))) break;
+            } else {
               if (!(ok = mbar_wait(bar(S::KFULL + st1), ph1))) break;
               tc::fence_after();
               issue_s(0, st1);
@@ -359,8 +388,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc::fence_after();
             issue_pv(1, st, i == 0);
             tc::commit(bar(S::VEMPTY + st));
-            if (last) tc::commit(bar(S::ODONE + 1));
-            if (!last) {
+            if (last) {
+              tc::commit(bar(S::ODONE + 1));
+              if (next.kind == 0) {
+                if (!(ok = start_tile(1, next, g + n, v + 1))) break;
+                next_started = true;
+              }
+            } else {
               issue_s(1, st1);
               tc::commit(bar(S::SFULL + 1));
               tc::commit(bar(S::KEMPTY + st1));
