@@ -980,16 +980,21 @@ def run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_r
     ms = timed([lambda: ops.last_token_logits(hid, cu, lm, nw, 1e-5, normed_out=normed,
                                               logits_out=logits)], 20)
     host = torch.empty(B, vocab, dtype=torch.float32, pin_memory=True)
-    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    r0.record(stream)
-    host.copy_(logits, non_blocking=True)
-    r1.record(stream)
+    host.copy_(logits, non_blocking=True)  # first touch of the pinned pages, untimed
     torch.cuda.synchronize()
+    copies = []
+    for _ in range(7):
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        host.copy_(logits, non_blocking=True)
+        r1.record(stream)
+        torch.cuda.synchronize()
+        copies.append(r0.elapsed_time(r1))
     lbytes = vocab * hidden * 2
     res["logits_c2_batch"] = {"sequences": B, "vocab": vocab, "ms": round(ms, 4),
                               "weight_gbps": round(lbytes / ms / 1e6, 1),
                               "weight_frac_of_measured_hbm_peak": round(lbytes / ms / 1e6 / hbm_peak, 4),
-                              "readback_ms": round(r0.elapsed_time(r1), 4),
+                              "readback_ms": round(sorted(copies)[3], 4),
                               "readback_bytes": B * vocab * 4}
     assert ops.device_status() == 0
     return res

@@ -1,5 +1,5 @@
 // Generic paged attention: any element type, any head_dim <= 256, any block_size <= 1024,
-// any n_rep, any number of query tokens per sequence. One CTA of 8 warps per (query token,
+// any n_rep, any number of query tokens per sequence. One CTA of 16 warps per (query token,
 // query head); the warps fold interleaved blocks and merge their states at the end.
 //
 // This is the per-row form of backend::cpu::paged_attention (src/backend/cpu.rs:57-112): the
@@ -34,9 +34,10 @@ struct GenericParams {
   float scale;
 };
 
-constexpr int kGenericWarps = 8;
+constexpr int kGenericWarps = 16;
 constexpr int kGenericThreads = kGenericWarps * 32;
 constexpr int kGenericMaxDim = 256;
+constexpr int kSmallRows = 16;  // register path: blocks of <= 16 rows, head_dim <= 64
 
 // Shared memory: q [kGenericMaxDim] | per-warp probabilities [kGenericWarps][block_size] |
 // per-warp partial accumulators [kGenericWarps][kGenericMaxDim] | per-warp max and sum.
@@ -45,13 +46,13 @@ __host__ __device__ constexpr size_t generic_smem_floats(int block_size) {
          size_t(kGenericWarps) * kGenericMaxDim + 2 * kGenericWarps;
 }
 
-// Each warp folds its own blocks (b = warp, warp + 8, ...) with the reference's block-wise
+// Each warp folds its own blocks (b = warp, warp + 16, ...) with the reference's block-wise
 // online softmax (scores of the block, block max, one correction, p = exp(s - max), sum, then
 // acc = acc * corr + sum_j p_j v_j), lanes over the block's rows for the scores and over
-// head_dim for the accumulation; the 8 partial states are merged at the end. Only blocks up to
+// head_dim for the accumulation; the 16 partial states are merged at the end. Only blocks up to
 // the last visible position are folded, so every folded block holds at least one visible key.
 template <typename T>
-__global__ void __launch_bounds__(kGenericThreads) generic_attn_kernel(const GenericParams p) {
+__global__ void __launch_bounds__(kGenericThreads, 1) generic_attn_kernel(const GenericParams p) {
   extern __shared__ float gsm[];
   const int D = p.head_dim, BS = p.block_size;
   float *qs = gsm;                                        // [D]
@@ -106,24 +107,93 @@ __global__ void __launch_bounds__(kGenericThreads) generic_attn_kernel(const Gen
   const int nb = limit / BS + 1;  // blocks holding a visible key
   const int32_t *table = p.block_tables + size_t(s) * p.max_blocks_per_seq;
   bool bad_id = false;
+  // This lane's query values: head_dim element lane + 32 k.
+  float qv[kPerLane];
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k) qv[k] = lane + 32 * k < D ? qs[lane + 32 * k] : 0.f;
+  // Blocks of <= 16 rows with head_dim <= 64 (e.g. Qwen2.5-0.5B's f32 pool) take a register
+  // path: the whole K and V block is loaded in one round trip, and the next block's id is
+  // fetched while this one is folded.
+  const bool small = BS <= kSmallRows && D <= 64;
+  int next_id = warp < nb ? table[warp] : 0;
   for (int b = warp; b < nb; b += kGenericWarps) {
-    int id = table[b];
+    int id = next_id;
+    if (b + kGenericWarps < nb) next_id = table[b + kGenericWarps];
     if (uint32_t(id) >= uint32_t(p.num_blocks)) { bad_id = true; id = 0; }
     const int kv_start = b * BS;
     const int bn = min(BS, L - kv_start);
     const size_t base = (size_t(id) * p.num_kv_heads + kh) * BS * size_t(D);
-    // Scores of this block (cpu.rs:84-94): lane r takes rows r, r + 32, ...
-    float bmax = neg_inf();
-    for (int j = lane; j < bn; j += 32) {
-      const T *kr = kc + base + size_t(j) * D;
-      float dot = 0.f;
-      for (int x = 0; x < D; ++x) dot = fmaf(qs[x], Elem<T>::to_f(kr[x]), dot);
-      const float sc = (kv_start + j > limit) ? neg_inf() : dot * p.scale;
-      pw[j] = sc;
-      bmax = fmaxf(bmax, sc);
-    }
+    if (small) {
+      float kr[kSmallRows][2], vr[kSmallRows][2];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+      for (int j = 0; j < kSmallRows; ++j)
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const bool in = j < bn && lane + 32 * k < D;
+          const size_t off = base + size_t(j) * D + lane + 32 * k;
+          kr[j][k] = in ? Elem<T>::to_f(kc[off]) : 0.f;
+          vr[j][k] = in ? Elem<T>::to_f(vc[off]) : 0.f;
+        }
+      float sc[kSmallRows];
+#pragma unroll
+      for (int j = 0; j < kSmallRows; ++j) sc[j] = fmaf(qv[0], kr[j][0], qv[1] * kr[j][1]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < kSmallRows; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], o);
+      // Every lane holds every score (the xor tree gives bit-identical sums), so the fold below
+      // runs redundantly per lane with no shared-memory round trip.
+      float bmax = neg_inf();
+#pragma unroll
+      for (int j = 0; j < kSmallRows; ++j) {
+        sc[j] = (j < bn && kv_start + j <= limit) ? sc[j] * p.scale : neg_inf();
+        bmax = fmaxf(bmax, sc[j]);
+      }
+      const float new_max = fmaxf(m, bmax);
+      const float corr = expf(m - new_max);
+      float psum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) acc[k] *= corr;
+#pragma unroll
+      for (int j = 0; j < kSmallRows; ++j) {
+        const float pj = j < bn ? expf(sc[j] - new_max) : 0.f;
+        psum += pj;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) acc[k] = fmaf(pj, vr[j][k], acc[k]);
+      }
+      l = l * corr + psum;
+      m = new_max;
+      continue;
+    }
+    // Scores of this block (cpu.rs:84-94): lanes over head_dim (coalesced row loads), four rows
+    // in flight, each dot product completed by a warp all-reduce.
+    float bmax = neg_inf();
+    for (int j0 = 0; j0 < bn; j0 += 4) {
+      float dot[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        dot[r] = 0.f;
+        if (j0 + r < bn) {
+          const T *kr = kc + base + size_t(j0 + r) * D;
+#pragma unroll
+          for (int k = 0; k < kPerLane; ++k)
+            if (lane + 32 * k < D) dot[r] = fmaf(qv[k], Elem<T>::to_f(kr[lane + 32 * k]), dot[r]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) dot[r] += __shfl_xor_sync(0xffffffffu, dot[r], o);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if (j0 + r < bn) {
+          const float sc = (kv_start + j0 + r > limit) ? neg_inf() : dot[r] * p.scale;
+          if (lane == 0) pw[j0 + r] = sc;
+          bmax = fmaxf(bmax, sc);
+        }
+      }
+    }
+    __syncwarp();
     // Fold (cpu.rs:96-105): bmax is finite (row kv_start <= limit is visible).
     const float new_max = fmaxf(m, bmax);
     const float corr = expf(m - new_max);
@@ -138,6 +208,7 @@ __global__ void __launch_bounds__(kGenericThreads) generic_attn_kernel(const Gen
     __syncwarp();
 #pragma unroll
     for (int k = 0; k < kPerLane; ++k) acc[k] *= corr;
+#pragma unroll 4
     for (int j = 0; j < bn; ++j) {
       const float pj = pw[j];
       const T *vr = vc + base + size_t(j) * D;

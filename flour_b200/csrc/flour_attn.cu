@@ -458,10 +458,16 @@ fa_status make_gemm_map(CUtensorMap *map, const void *base, int64_t rows, int64_
   return FA_OK;
 }
 
-// 256-column output tiles when they alone fill the GPU, else 128 (more CTAs for small M).
+// 256-column output tiles when they alone fill the GPU, else 128 (more CTAs for small M). With
+// several waves, 128 also wins when it cuts the columns of the busiest SM by more than 10 %
+// (weight-streaming shapes such as a 64-row lm_head over a 128K vocabulary: 4 x 256 = 1024
+// columns against 7 x 128 = 896).
 int gemm_bn(int M, int N) {
-  const int64_t tiles256 = int64_t((M + 127) / 128) * ((N + 255) / 256);
-  return tiles256 >= sm_count() ? 256 : 128;
+  const int64_t m_tiles = (M + 127) / 128, sms = sm_count();
+  const int64_t tiles256 = m_tiles * ((N + 255) / 256), tiles128 = m_tiles * ((N + 127) / 128);
+  if (tiles256 < sms) return 128;
+  const int64_t cols256 = (tiles256 + sms - 1) / sms * 256, cols128 = (tiles128 + sms - 1) / sms * 128;
+  return cols128 * 10 < cols256 * 9 ? 128 : 256;
 }
 
 template <typename T, int BN, class Epi>
