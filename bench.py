@@ -726,16 +726,17 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
     """C5 mixed serving step: Qwen2-7B heads (Hq=28, Hkv=4, d=128), 28 layers, 512 sequences
     (ctx ~ LogNormal(ln 1024, 0.8) capped at 8192); about 10 % are new prompts of L ~ U[256, 2048]
     run as prefill, the rest decode one token. The sequences are partitioned longest-first over
-    the ranks, so the total work is fixed as N grows (strong scaling). One step = per layer:
+    the ranks (prompts first, then decode sequences where the two-stream step time grows least), so
+    the total work is fixed as N grows (strong scaling). One step = per layer:
     the decode sequences' new K/V write + decode (one fa_paged_decode_append launch) on one
     stream, the prefill sequences' reshape_and_cache and the prefill launch on a second stream
     (the two sub-batches share no data); each rank owns its
     own pools. KV values are zero-filled (timing only; the kernels' arithmetic does not depend on
     the values)."""
-    from flour_b200.workloads import QWEN7B, c5_plan, lpt_partition, make_decode, make_prefill
+    from flour_b200.workloads import QWEN7B, c5_plan, make_decode, make_prefill, mixed_partition
     h, L = QWEN7B, 28
     ctx, is_pf, pf_len, cost = c5_plan(args.seed)
-    mine = lpt_partition(cost, world)[rank]
+    mine = mixed_partition(cost, is_pf, world)[rank]
     dec = [i for i in mine if not is_pf[i]]
     pf = [i for i in mine if is_pf[i]]
     scale = 1.0 / math.sqrt(h.head_dim)

@@ -258,22 +258,60 @@ def make_prefill(heads: Heads, lens, prefix, dtype: torch.dtype, device, seed: i
                         int(lens.max()) if len(lens) else 0, total)
 
 
+# Per-unit times of the C5 step on one B200, fitted to a measured 8-rank step (Qwen2-7B heads):
+# a decode sequence costs its context length x _C5_DECODE_S_PER_TOKEN per layer; a prompt costs
+# its prefill work units x _C5_PREFILL_S_PER_UNIT, where a unit is one 128-token KV tile of one
+# work item (a 2 x TQ-token chunk and one KV head) and each item adds _C5_ITEM_UNITS units for
+# its epilogue. Short prompts are dearer than their FLOPs because of that per-item cost.
+_C5_DECODE_S_PER_TOKEN = 5.5e-10
+_C5_PREFILL_S_PER_UNIT = 1.51e-8
+_C5_ITEM_UNITS = 3
+
+
+def prefill_units(S: int, heads: Heads, prefix: int = 0, tile: int = 128) -> int:
+    """Work units of the tcgen05 prefill kernel for one prompt of S new tokens after `prefix`
+    cached ones: per (chunk of 2 * (128 // n_rep) tokens, KV head) item, its KV tiles plus the
+    epilogue's share."""
+    chunk = 2 * (128 // heads.n_rep)
+    units = 0
+    for t0 in range(0, S, chunk):
+        kv_end = prefix + min(t0 + chunk, S)
+        units += -(-kv_end // tile) + _C5_ITEM_UNITS
+    return units * heads.num_kv_heads
+
+
 def c5_plan(seed: int, n: int = 512, prefill_frac: float = 0.1):
     """C5 mixed serving step (Qwen2-7B heads): 512 sequences with ctx ~ LogNormal(ln 1024, 0.8)
     capped at 8192; a prefill_frac share are new prompts of L ~ U[256, 2048] (no cached prefix),
-    the rest decode one token. Returns (ctx, is_prefill, prefill_len, cost) where cost is an
-    estimated time per sequence (decode: KV bytes at HBM speed; prefill: causal FLOPs at tensor
-    speed) for longest-first partitioning across GPUs."""
+    the rest decode one token. Returns (ctx, is_prefill, prefill_len, cost) where cost is the
+    estimated time per layer of each sequence on one GPU (decode: per context token; prefill: per
+    kernel work unit, see prefill_units), for partitioning across GPUs."""
     rng = np.random.default_rng(seed + 55)
     ctx = c5_contexts(seed, n)
     is_pf = rng.random(n) < prefill_frac
     pf_len = rng.integers(256, 2049, size=n)
-    h = QWEN7B
-    kv_bytes_per_token = h.num_kv_heads * h.head_dim * 2 * 2
-    dec_cost = ctx * kv_bytes_per_token / 6.4e12
-    pf_cost = 4.0 * h.num_heads * h.head_dim * pf_len * (pf_len + 1) / 2 / 7.0e14 + \
-        pf_len * kv_bytes_per_token / 6.4e12
+    dec_cost = ctx * _C5_DECODE_S_PER_TOKEN
+    pf_cost = np.array([prefill_units(int(x), QWEN7B) * _C5_PREFILL_S_PER_UNIT for x in pf_len])
     return ctx, is_pf, pf_len, np.where(is_pf, pf_cost, dec_cost)
+
+
+def mixed_partition(costs, is_prefill, parts: int, overlap: float = 0.5) -> list[list[int]]:
+    """Sequence sharding for a step whose decode and prefill sub-batches run on two streams of
+    each GPU: a GPU with prefill time P and decode time D takes about max(P, D) + overlap *
+    min(P, D). Prompts are placed first (longest-first, the larger and coarser work), then each
+    decode sequence, longest first, goes where that estimate grows least."""
+    costs = np.asarray(costs, dtype=np.float64)
+    is_prefill = np.asarray(is_prefill, dtype=bool)
+    pf = np.flatnonzero(is_prefill)
+    bins = [[int(pf[j]) for j in b] for b in lpt_partition(costs[pf], parts)]
+    P = [float(costs[b].sum()) for b in bins]
+    D = [0.0] * parts
+    for i in np.flatnonzero(~is_prefill)[np.argsort(-costs[~is_prefill], kind="stable")]:
+        est = [max(P[r], D[r] + costs[i]) + overlap * min(P[r], D[r] + costs[i]) for r in range(parts)]
+        r = int(np.argmin(est))
+        bins[r].append(int(i))
+        D[r] += float(costs[i])
+    return [sorted(b) for b in bins]
 
 
 def lpt_partition(costs, parts: int) -> list[list[int]]:

@@ -6,7 +6,8 @@ import pytest
 import torch
 
 from flour_b200.paged import BlockAllocator, BlockTable, build_batch
-from flour_b200.workloads import lpt_partition, make_c3, c5_contexts
+from flour_b200.workloads import (QWEN7B, c5_contexts, c5_plan, lpt_partition, make_c3,
+                                  mixed_partition, prefill_units)
 
 
 def test_allocator_hands_out_distinct_blocks_then_exhausts():  # paged.rs:343-353
@@ -78,6 +79,31 @@ def test_lpt_partition_balances_lognormal_contexts():
     assert sorted(i for p in parts for i in p) == list(range(len(ctx)))
     loads = [ctx[p].sum() for p in parts]
     assert max(loads) / min(loads) < 1.02
+
+
+def test_mixed_partition_balances_two_stream_steps():
+    ctx, is_pf, _, cost = c5_plan(1000)
+
+    def step(b, overlap=0.5):
+        p = cost[[i for i in b if is_pf[i]]].sum()
+        d = cost[[i for i in b if not is_pf[i]]].sum()
+        return max(p, d) + overlap * min(p, d)
+
+    for world in (1, 2, 4, 8):
+        parts = mixed_partition(cost, is_pf, world)
+        assert sorted(i for p in parts for i in p) == list(range(len(ctx)))
+        new = max(step(b) for b in parts)
+        old = max(step(b) for b in lpt_partition(cost, world))
+        assert new <= old * 1.0001
+        assert new <= min(step(b) for b in parts) * 1.01  # within 1 % across ranks
+
+
+def test_prefill_units_count_tiles_and_items():
+    # Qwen2-7B: n_rep 7 -> 18-token Q tiles, 36-token chunks; 4 KV heads.
+    assert prefill_units(36, QWEN7B) == (1 + 3) * 4
+    assert prefill_units(37, QWEN7B) == (1 + 3 + 1 + 3) * 4
+    # a cached prefix adds KV tiles to every chunk
+    assert prefill_units(36, QWEN7B, prefix=128) == (2 + 3) * 4
 
 
 def test_c3_generator_shares_prefix_blocks():
