@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("C2"): Llama-3-8B heads (32 q / 8 kv, head_dim 128),
+Workload (the headline configuration, "C2"): Llama-3-8B heads (32 q / 8 kv, head_dim 128),
 block_size 16, 32 layers with their own pools, batch 64, context lengths ~ U[512, 4096],
 bf16 KV ~ N(0,1), shuffled non-contiguous block tables. One step = one decode step of the
 batch: for each of the 32 layers, the write of the 64 new tokens' K/V into their slots followed by
