@@ -92,6 +92,7 @@ struct QkvEpilogue {
   const int32_t *positions, *slots;  // [M]
   float rms_eps;
   int32_t num_heads, num_kv_heads, head_dim, num_blocks, block_size, max_position;
+  static constexpr bool kChunked = false;  // RoPE and the q/k norms need whole heads
 
   // One row (token) of a 128 x BN tile: BN / head_dim whole heads starting at column col0.
   template <int BN, class Acc>
@@ -193,6 +194,26 @@ template <typename T>
 struct ResidualEpilogue {
   T *out;                 // [M, N]
   const T *residual;      // [M, N] or null
+  static constexpr bool kChunked = true;  // 32-column chunks are independent
+
+  __device__ void apply32(float (&v)[32], int row, int col, const GemmShape &s) const {
+    const size_t base = size_t(row) * s.N + col;
+    if (residual) {
+      const uint4 *rp = reinterpret_cast<const uint4 *>(residual + base);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = rp[q];
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack2<T>(ww[j]);
+          v[q * 8 + 2 * j] += f.x;
+          v[q * 8 + 2 * j + 1] += f.y;
+        }
+      }
+    }
+    store32<T>(out + base, v);
+  }
 
   template <int BN, class Acc>
   __device__ void operator()(const Acc &acc, int row, int col0, const GemmShape &s) const {
@@ -202,24 +223,18 @@ struct ResidualEpilogue {
       if (col >= s.N) break;
       float v[32];
       acc.ld32(c * 32, v);
-      if (!row_ok) continue;
-      const size_t base = size_t(row) * s.N + col;
-      if (residual) {
-        const uint4 *rp = reinterpret_cast<const uint4 *>(residual + base);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 w = rp[q];
-          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = unpack2<T>(ww[j]);
-            v[q * 8 + 2 * j] += f.x;
-            v[q * 8 + 2 * j + 1] += f.y;
-          }
-        }
-      }
-      store32<T>(out + base, v);
+      if (row_ok) apply32(v, row, col, s);
     }
+  }
+
+  // Chunk c (32 columns) of a row whose accumulator is in shared memory (split-K path).
+  template <class Acc>
+  __device__ void chunk(const Acc &acc, int row, int col0, int c, const GemmShape &s) const {
+    const int col = col0 + c * 32;
+    if (row >= s.M || col >= s.N) return;
+    float v[32];
+    acc.ld32(c * 32, v);
+    apply32(v, row, col, s);
   }
 };
 
@@ -227,6 +242,13 @@ struct ResidualEpilogue {
 // engine, engine.rs:221-222).
 struct F32Epilogue {
   float *out;  // [M, N], N % 32 == 0, 16-byte aligned
+  static constexpr bool kChunked = true;  // 32-column chunks are independent
+
+  __device__ void apply32(const float (&v)[32], int row, int col, const GemmShape &s) const {
+    float4 *d = reinterpret_cast<float4 *>(out + size_t(row) * s.N + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
 
   template <int BN, class Acc>
   __device__ void operator()(const Acc &acc, int row, int col0, const GemmShape &s) const {
@@ -236,11 +258,18 @@ struct F32Epilogue {
       if (col >= s.N) break;
       float v[32];
       acc.ld32(c * 32, v);
-      if (!row_ok) continue;
-      float4 *d = reinterpret_cast<float4 *>(out + size_t(row) * s.N + col);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      if (row_ok) apply32(v, row, col, s);
     }
+  }
+
+  // Chunk c (32 columns) of a row whose accumulator is in shared memory (split-K path).
+  template <class Acc>
+  __device__ void chunk(const Acc &acc, int row, int col0, int c, const GemmShape &s) const {
+    const int col = col0 + c * 32;
+    if (row >= s.M || col >= s.N) return;
+    float v[32];
+    acc.ld32(c * 32, v);
+    apply32(v, row, col, s);
   }
 };
 
@@ -614,9 +643,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
-    if (ok && t < rows) {
-      const int row = row0 + t;
-      epi.template operator()<BN>(LocalAcc{part + row * kPitch}, m * 128 + row, n * BN, s);
+    if (ok) {
+      if constexpr (Epi::kChunked) {
+        // One 32-column chunk per thread: every epilogue thread works, not one per row.
+        constexpr int kChunks = BN / 32;
+        for (int u = t; u < rows * kChunks; u += 128) {
+          const int row = row0 + u / kChunks;
+          epi.chunk(LocalAcc{part + row * kPitch}, m * 128 + row, n * BN, u % kChunks, s);
+        }
+      } else if (t < rows) {
+        const int row = row0 + t;
+        epi.template operator()<BN>(LocalAcc{part + row * kPitch}, m * 128 + row, n * BN, s);
+      }
     }
   }
   tc::fence_before();
