@@ -487,16 +487,16 @@ fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, cons
 }
 
 // Split-K over a cluster of `ranks` CTAs per 128 x 128 tile (one tile per cluster).
-template <typename T, class Epi>
-fa_status launch_gemm_splitk(int M, int N, int K, int ranks, const Epi &epi, const void *a,
-                             const void *b, int32_t dt, cudaStream_t stream, const char *who) {
+template <typename T, int AROWS, class Epi>
+fa_status launch_gemm_splitk_rows(int M, int N, int K, int ranks, const Epi &epi, const void *a,
+                                  const void *b, int32_t dt, cudaStream_t stream, const char *who) {
   constexpr int BN = 128;
-  using C = fa::GemmCfg<BN>;
+  using C = fa::GemmCfg<BN, AROWS>;
   fa::GemmShape s{M, N, K, (M + 127) / 128, (N + BN - 1) / BN};
   CUtensorMap ta, tb;
-  if (fa_status st = make_gemm_map(&ta, a, M, K, dt, 128, who); st != FA_OK) return st;
+  if (fa_status st = make_gemm_map(&ta, a, M, K, dt, AROWS, who); st != FA_OK) return st;
   if (fa_status st = make_gemm_map(&tb, b, N, K, dt, BN, who); st != FA_OK) return st;
-  auto kern = fa::gemm_tn_splitk_kernel<T, BN, Epi>;
+  auto kern = fa::gemm_tn_splitk_kernel<T, BN, Epi, AROWS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "%s: set smem attribute: %s", who, cudaGetErrorString(e));
   cudaLaunchConfig_t cfg{};
@@ -514,6 +514,14 @@ fa_status launch_gemm_splitk(int M, int N, int K, int ranks, const Epi &epi, con
   e = cudaLaunchKernelEx(&cfg, kern, s, epi, ta, tb);
   if (e != cudaSuccess) return fail(FA_ECUDA, "%s: cluster launch: %s", who, cudaGetErrorString(e));
   return check_launch(who);
+}
+
+// Decode-sized batches (M <= 64) load 64-row A boxes: 8 ring stages instead of 6.
+template <typename T, class Epi>
+fa_status launch_gemm_splitk(int M, int N, int K, int ranks, const Epi &epi, const void *a,
+                             const void *b, int32_t dt, cudaStream_t stream, const char *who) {
+  if (M <= 64) return launch_gemm_splitk_rows<T, 64>(M, N, K, ranks, epi, a, b, dt, stream, who);
+  return launch_gemm_splitk_rows<T, 128>(M, N, K, ranks, epi, a, b, dt, stream, who);
 }
 
 // How many CTAs split K when 128-wide tiles leave most SMs idle (1 = no split). Clusters need

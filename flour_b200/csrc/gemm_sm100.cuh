@@ -28,11 +28,16 @@ namespace fa {
 constexpr int kGemmBK = 64;          // K per ring stage: one 128-byte swizzled row per operand row
 constexpr int kGemmThreads = 192;    // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
 
-template <int BN>
+// AROWS = 64 (split-K with M <= 64 only): the A stage holds 64 rows, so the ring takes 8 stages
+// instead of 6 (more weight bytes in flight per SM). The M = 128 MMA still reads 128 A rows; rows
+// 64-127 then fall on the same stage's B bytes and only feed accumulator rows >= 64, which the
+// epilogue never stores.
+template <int BN, int AROWS = 128>
 struct GemmCfg {
   static_assert(BN == 128 || BN == 256, "BN is 128 or 256");
-  static constexpr int kStages = BN == 256 ? 4 : 6;
-  static constexpr int kABytes = 128 * kGemmBK * 2;
+  static_assert(AROWS == 128 || (AROWS == 64 && BN == 128), "64-row A stages only at BN = 128");
+  static constexpr int kStages = BN == 256 ? 4 : (AROWS == 64 ? 8 : 6);
+  static constexpr int kABytes = AROWS * kGemmBK * 2;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int FULL = 0, EMPTY = kStages, AFULL = 2 * kStages, AEMPTY = AFULL + 2,
@@ -506,12 +511,12 @@ struct LocalAcc {
   }
 };
 
-template <typename T, int BN, class Epi>
+template <typename T, int BN, class Epi, int AROWS = 128>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_splitk_kernel(const __grid_constant__ GemmShape s, const __grid_constant__ Epi epi,
                           const __grid_constant__ CUtensorMap tm_a,
                           const __grid_constant__ CUtensorMap tm_b) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, AROWS>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int kPitch = BN + 4;  // f32 row pitch of the partial (bank-conflict padding)
   static_assert(128 * kPitch * 4 <= C::kBarOff, "partial must fit in the operand ring");

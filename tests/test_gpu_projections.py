@@ -96,7 +96,7 @@ def check_qkv(c, q, kc0, vc0, eps=1e-6):
     close(kc[blk, :, off, :], kcand[live], 3e-2, 2e-2)
 
 
-@pytest.mark.parametrize("T", [1, 129, 300])
+@pytest.mark.parametrize("T", [1, 64, 129, 300])
 def test_qkv_llama_heads(device, T):
     c = make_qkv(device, T, 512, 8, 2, 128, seed=T)
     check_qkv(c, *run_qkv(c))
@@ -160,7 +160,8 @@ def test_qkv_rejects_bad_arguments(device):
     assert e.value.status == _lib.FA_EUNSUPPORTED
 
 
-@pytest.mark.parametrize("T,fin,fout", [(1, 4096, 4096), (300, 4096, 4096), (129, 896, 896),
+@pytest.mark.parametrize("T,fin,fout", [(1, 4096, 4096), (64, 4096, 4096), (65, 4096, 4096),
+                                        (300, 4096, 4096), (129, 896, 896),
                                         (8192, 896, 896), (2000, 3584, 3584)])
 def test_o_proj_residual_vs_torch_fp32(device, T, fin, fout):
     g = torch.Generator(device=device).manual_seed(T + fin)
