@@ -524,22 +524,68 @@ fa_status launch_gemm_splitk(int M, int N, int K, int ranks, const Epi &epi, con
   return launch_gemm_splitk_rows<T, 128>(M, N, K, ranks, epi, a, b, dt, stream, who);
 }
 
-// How many CTAs split K when 128-wide tiles leave most SMs idle (1 = no split). Clusters need
-// their CTAs inside one GPC; measured on B200 (64 tokens, Llama-3-8B projections), splits that
-// keep the grid near 2/3 of the SMs schedule in one wave, larger ones spill into a second.
+// How many clusters of `ranks` split-K CTAs can be resident at once (the driver's answer, which
+// includes placing each cluster inside one GPC), cached per device and cluster size.
+template <typename T, int AROWS, class Epi>
+int splitk_max_clusters(int ranks) {
+  static std::mutex mu;
+  static std::unordered_map<int64_t, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const int64_t key = int64_t(dev) * 64 + ranks;
+  std::lock_guard<std::mutex> lock(mu);
+  if (auto it = cache.find(key); it != cache.end()) return it->second;
+  using C = fa::GemmCfg<128, AROWS>;
+  auto kern = fa::gemm_tn_splitk_kernel<T, 128, Epi, AROWS>;
+  int n = 0;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+  if (e == cudaSuccess) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(ranks));
+    cfg.blockDim = dim3(fa::kGemmThreads);
+    cfg.dynamicSmemBytes = C::kAlloc;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(ranks);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+  }
+  if (e != cudaSuccess) {  // a failed query only means "no split"
+    n = 0;
+    cudaGetLastError();
+  }
+  cache[key] = n;
+  return n;
+}
+
+// How many CTAs split K when 128-wide tiles leave most SMs idle (1 = no split): the largest
+// split, at least 4 K blocks per CTA, whose clusters all fit on the GPU at once. Clusters live
+// inside one GPC, so the fit depends on the cluster size and not only on the CTA count (on B200,
+// 32 tiles x 4 = 128 CTAs fit in one wave, 48 tiles x 3 = 144 do not).
+template <typename T, class Epi>
 int gemm_split_ranks(int M, int N, int K) {
   const int64_t tiles = int64_t((M + 127) / 128) * ((N + 127) / 128);
   const int num_k = (K + fa::kGemmBK - 1) / fa::kGemmBK;
-  const int64_t target = std::max(1, sm_count() * 2 / 3);
-  int r = int(std::min<int64_t>(fa::kSplitMaxRanks, target / std::max<int64_t>(1, tiles)));
-  r = std::min(r, num_k / 4);  // at least 4 K blocks per CTA
-  return r >= 2 ? r : 1;
+  const int64_t max_r = std::min<int64_t>(
+      std::min<int64_t>(fa::kSplitMaxRanks, num_k / 4), sm_count() / std::max<int64_t>(1, tiles));
+  for (int r = int(max_r); r >= 2; --r) {
+    const int fit = M <= 64 ? splitk_max_clusters<T, 64, Epi>(r)
+                            : splitk_max_clusters<T, 128, Epi>(r);
+    if (tiles <= fit) return r;
+  }
+  return 1;
 }
 
 template <typename T, class Epi>
 fa_status launch_gemm(int M, int N, int K, const Epi &epi, const void *a, const void *b,
                       int32_t dt, cudaStream_t stream, const char *who) {
-  if (const int r = gemm_split_ranks(M, N, K); r >= 2)
+  if (const int r = gemm_split_ranks<T, Epi>(M, N, K); r >= 2)
     return launch_gemm_splitk<T>(M, N, K, r, epi, a, b, dt, stream, who);
   if (gemm_bn(M, N) == 256) return launch_gemm_t<T, 256>(M, N, K, epi, a, b, dt, stream, who);
   return launch_gemm_t<T, 128>(M, N, K, epi, a, b, dt, stream, who);
