@@ -21,6 +21,7 @@ FA_DEVERR_TIMEOUT = 0x8
 FA_DEVERR_SEQLEN = 0x10
 FA_DEVERR_PAIR = 0x20
 FA_DEVERR_POSITION = 0x40
+FA_DEVERR_LAUNCH = 0x80
 FA_MAX_COPY_LAYERS = 128
 FA_NOALLOC_DECODE_SCRATCH_BYTES = 8 * 1024 * 1024
 

@@ -43,19 +43,17 @@ def needs_build() -> bool:
     return any(s.stat().st_mtime > t for s in sources())
 
 
-def build(verbose: bool = False, force: bool = False, out: Path | None = None,
-          defines: tuple[str, ...] = ()) -> Path:
-    """Compile the library to `out` (default: the in-tree libflour_attn.so). `defines` are extra
-    -D tuning values (e.g. "FA_PF_POLY_EVERY=2") for building variants outside the tree."""
+def build(verbose: bool = False, force: bool = False, out: Path | None = None) -> Path:
+    """Compile the library to `out` (default: the in-tree libflour_attn.so); the in-tree build
+    is skipped when the library is newer than every source."""
     target = Path(out) if out is not None else LIB
-    if out is None and not defines and not force and not needs_build():
+    if out is None and not force and not needs_build():
         return LIB
     cmd = [
         nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
         "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
         "-I", str(ROOT / "include"), "-I", str(CSRC), "-I", str(HOST),
         "-cudart", "static",
-        *[f"-D{d}" for d in defines],
         "-o", str(target), str(CSRC / "flour_attn.cu"), str(HOST / "flour_host.cpp"),
     ]
     if verbose:

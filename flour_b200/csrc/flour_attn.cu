@@ -6,6 +6,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
+#include <cstdint>
 #include <mutex>
 #include <unordered_map>
 
@@ -179,25 +181,41 @@ constexpr int kDecodeStages = 3;
 
 // Split-K merge tickets must be zero when a decode launch starts. Every launch returns its own
 // tickets to zero, but a caller workspace reused with another shape may hold split-K partials
-// where the new tickets go. Per workspace base pointer, remember the smallest ticket region of
-// any launch so far: the bytes below it are zero after every launch (and after every CUDA-graph
-// replay of a captured one); a launch whose tickets reach past it zeroes the difference first.
+// where the new tickets go (a launch's partials start right after its own tickets). Per
+// workspace base pointer the library keeps:
+//   clean:    a prefix that is zero whenever the next launch starts;
+//   captured: the smallest ticket region of any launch recorded into a CUDA graph. A replay can
+//             come at any time and leaves partials from that offset on, so `clean` never rises
+//             above it.
+// A launch with a smaller ticket region lowers `clean` to its own (its partials follow); one
+// that reaches past `clean` zeroes the difference first, after which (when that memset runs
+// eagerly, not into a graph) the prefix is clean up to its region, or to `captured`.
+struct TicketState {
+  size_t clean;
+  size_t captured;
+};
 std::mutex g_ticket_mu;
-std::unordered_map<uintptr_t, size_t> g_ticket_clean;
+std::unordered_map<uintptr_t, TicketState> g_ticket_state;
 
 fa_status zero_stale_tickets(void *ws, size_t ticket_bytes, cudaStream_t stream) {
-  size_t clean;
-  {
-    std::lock_guard<std::mutex> lock(g_ticket_mu);
-    const auto [it, fresh] = g_ticket_clean.try_emplace(reinterpret_cast<uintptr_t>(ws), ticket_bytes);
-    if (fresh) return FA_OK;  // a workspace is zero-filled before its first use
-    clean = it->second;
-    if (ticket_bytes < clean) it->second = ticket_bytes;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess)
+    return fail(FA_ECUDA, "decode: cudaStreamIsCapturing failed");
+  const bool capturing = cap != cudaStreamCaptureStatusNone;
+  std::lock_guard<std::mutex> lock(g_ticket_mu);
+  const TicketState init{ticket_bytes, capturing ? ticket_bytes : SIZE_MAX};
+  const auto [it, fresh] = g_ticket_state.try_emplace(reinterpret_cast<uintptr_t>(ws), init);
+  if (fresh) return FA_OK;  // a workspace is zero-filled before its first use
+  TicketState &s = it->second;
+  if (capturing) s.captured = std::min(s.captured, ticket_bytes);
+  if (ticket_bytes <= s.clean) {
+    s.clean = ticket_bytes;
+    return FA_OK;
   }
-  if (ticket_bytes <= clean) return FA_OK;
   const cudaError_t e =
-      cudaMemsetAsync(static_cast<char *>(ws) + clean, 0, ticket_bytes - clean, stream);
+      cudaMemsetAsync(static_cast<char *>(ws) + s.clean, 0, ticket_bytes - s.clean, stream);
   if (e != cudaSuccess) return fail(FA_ECUDA, "decode: zeroing merge tickets: %s", cudaGetErrorString(e));
+  if (!capturing) s.clean = std::min(ticket_bytes, s.captured);
   return FA_OK;
 }
 

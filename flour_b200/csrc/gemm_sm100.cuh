@@ -31,7 +31,7 @@ constexpr int kGemmThreads = 192;    // warp 0 TMA, warp 1 MMA + TMEM owner, war
 // AROWS = 64 (split-K with M <= 64 only): the A stage holds 64 rows, so the ring takes 8 stages
 // instead of 6 (more weight bytes in flight per SM). The M = 128 MMA still reads 128 A rows; rows
 // 64-127 then fall on the same stage's B bytes and only feed accumulator rows >= 64, which the
-// epilogue never stores.
+// epilogue never stores. The kernel refuses (FA_DEVERR_LAUNCH, no work) a shape with M > 64.
 template <int BN, int AROWS = 128>
 struct GemmCfg {
   static_assert(BN == 128 || BN == 256, "BN is 128 or 256");
@@ -536,6 +536,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Barriers: FULL/EMPTY ring, AFULL (partial ready in TMEM), and AEMPTY reused as "every CTA's
   // partial is in its shared memory" (128 epilogue threads x nranks arrivals).
   const int PREADY = C::AEMPTY;
+  if (AROWS < 128 && s.M > AROWS) {  // uniform over the grid: every CTA leaves before any barrier
+    if (tid == 0 && blockIdx.x == 0) report(FA_DEVERR_LAUNCH);
+    return;
+  }
 
   if (tid == 0) {
     for (int i = 0; i < C::NBARS; ++i) mbar_init(bar(i), i == PREADY ? 128 * int(nranks) : 1);

@@ -73,6 +73,7 @@ typedef enum fa_dtype { FA_F32 = 0, FA_BF16 = 1, FA_F16 = 2 } fa_dtype;
 #define FA_DEVERR_SEQLEN 0x10    /* cu_seqlens_q not non-decreasing or past total_q */
 #define FA_DEVERR_PAIR 0x20      /* copy_blocks pair entry outside [0, num_blocks) */
 #define FA_DEVERR_POSITION 0x40  /* RoPE position outside [0, max_position) */
+#define FA_DEVERR_LAUNCH 0x80    /* a kernel refused a launch shape it does not support */
 
 /* One layer of the paged KV pool. */
 typedef struct fa_kv_layer {
@@ -204,9 +205,15 @@ FA_API fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *qu
  * process exits) and calls no allocating routine. Same arguments and results as
  * fa_paged_decode minus the workspace.
  *   - Requests whose split-K scratch would exceed FA_NOALLOC_DECODE_SCRATCH_BYTES are rejected
- *     with FA_ERANGE (use fa_paged_decode with a workspace for those).
+ *     with FA_ERANGE (use fa_paged_decode with a workspace for those). The test is exact: a call
+ *     is accepted when fa_paged_attention_workspace_size(num_seqs, num_heads, num_kv_heads,
+ *     head_dim, max_context_len, 1) <= FA_NOALLOC_DECODE_SCRATCH_BYTES, so a caller can ask in
+ *     advance. Shapes outside the fast decode path run the generic kernel, which needs no
+ *     scratch, and are never rejected for size.
  *   - The first call on each device looks up the buffer's device address (with that device
- *     current); make that first call before any stream capture.
+ *     current); make that first call before any stream capture. The address is kept for the
+ *     life of the process: a device reset (cudaDeviceReset, or a primary-context reset) after
+ *     that first call is not supported by this entry point.
  *   - All calls share the one buffer per device, so calls whose GPU work overlaps (different
  *     streams, or threads without ordering) race; order them on one stream. */
 #define FA_NOALLOC_DECODE_SCRATCH_BYTES (8u * 1024u * 1024u)

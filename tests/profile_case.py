@@ -1,10 +1,13 @@
-"""Small, fixed cases for Nsight Compute captures of one kernel.
+"""Profiling fixture: small, fixed cases for Nsight Compute captures of one kernel.
 
-    python -m flour_b200.profile_case decode  [--launches 3] [--batch 64] [--seed 1000]
-    python -m flour_b200.profile_case longctx [--launches 3]
-    python -m flour_b200.profile_case prefill [--launches 3]
-    python -m flour_b200.profile_case qkv     [--launches 3] [--tokens 13490]
-    python -m flour_b200.profile_case oproj   [--launches 3] [--tokens 13490]
+    python tests/profile_case.py decode  [--launches 3] [--batch 64] [--seed 1000]
+    python tests/profile_case.py longctx [--launches 3]
+    python tests/profile_case.py prefill [--launches 3]
+    python tests/profile_case.py qkv     [--launches 3] [--tokens 13490]
+    python tests/profile_case.py oproj   [--launches 3] [--tokens 13490]
+
+Not collected by pytest (no test_ prefix); the profiles/*.md summaries name the command line
+that made them.
 
 `decode` is one layer of the C2 configuration (64 sequences, ctx ~ U[512, 4096], ~0.6 GB of
 KV: larger than L2, a few GB at most on the device). `longctx` is 4 sequences of the C4
@@ -18,12 +21,15 @@ from __future__ import annotations
 
 import argparse
 import math
+import sys
+from pathlib import Path
 
 import numpy as np
 import torch
 
-from . import ops
-from .workloads import LLAMA8B, c2_contexts, c4_contexts, make_c3, make_decode
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+from flour_b200 import ops  # noqa: E402
+from flour_b200.workloads import LLAMA8B, c2_contexts, c4_contexts, make_c3, make_decode
 
 
 def main() -> int:
@@ -47,7 +53,7 @@ def main() -> int:
         torch.cuda.synchronize()
         print(f"{a.case}: {b.kv_bytes_per_layer() + b.io_bytes_per_layer()} algorithmic bytes/launch")
     elif a.case in ("qkv", "oproj"):
-        from .paged import rope_tables
+        from flour_b200.paged import rope_tables
         T, hidden, hq, hkv, d = a.tokens, 4096, 32, 8, 128
         g = torch.Generator(device=dev).manual_seed(a.seed)
         x = torch.randn(T, hidden, device=dev, generator=g).to(torch.bfloat16)

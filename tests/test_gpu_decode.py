@@ -138,6 +138,37 @@ def test_workspace_reused_across_shapes(device):
     assert ops.device_status() == 0
 
 
+def _memsets_during(fn):
+    """Number of device memsets that `fn` enqueues (CUDA activity trace)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    # Device-side activity only (the runtime API call is listed as a separate cudaMemsetAsync).
+    return sum(1 for e in prof.events()
+               if "memset" in e.name.lower() and not e.name.startswith("cuda"))
+
+
+def test_workspace_ticket_zeroing_is_paid_once(device):
+    # Eager large, small, large, large on one workspace: the first large call after the small one
+    # zeroes the tickets that land on the small call's partials; the next large call finds them
+    # clean and issues no memset. Every output equals a run on a fresh workspace.
+    small = make_decode(LLAMA8B, np.array([9000, 7000, 8000, 6000]), torch.bfloat16, device, 16)
+    big = make_decode(LLAMA8B, c2_contexts(17, batch=64), torch.bfloat16, device, 17)
+    want_small = run_decode(small, ops.Workspace(device)).clone()
+    want_big = run_decode(big, ops.Workspace(device)).clone()
+    ws = ops.Workspace(device)
+    ws.get(64 << 20)
+    assert torch.equal(run_decode(big, ws), want_big)
+    assert torch.equal(run_decode(small, ws), want_small)
+    got = {}
+    n1 = _memsets_during(lambda: got.setdefault("a", run_decode(big, ws).clone()))
+    n2 = _memsets_during(lambda: got.setdefault("b", run_decode(big, ws).clone()))
+    assert torch.equal(got["a"], want_big) and torch.equal(got["b"], want_big)
+    assert (n1, n2) == (1, 0)
+    assert ops.device_status() == 0
+
+
 def test_general_entry_dispatches_decode(device):
     ctx = np.random.default_rng(12).integers(100, 3000, size=6)
     b = make_decode(LLAMA8B, ctx, torch.bfloat16, device, 12)
