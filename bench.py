@@ -140,14 +140,28 @@ class ClockSampler:
                 if v.strip().lower() == "active":
                     reasons.add(n)
         load = [s for s, p in zip(sm, power) if p > 200.0] or sm
+        pload = [p for p in power if p > 200.0] or power
         return {"sm_mhz": statistics.median(load) if load else None,
                 "sm_max_mhz": max(smax) if smax else None,
+                "power_w": round(statistics.median(pload), 1) if pload else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # ---------------------------------------------------------------------------------------
 # reference arm: the reference's CPU paged attention (oracle restatement), host cores only
 # ---------------------------------------------------------------------------------------
+
+def cpu_model() -> str:
+    """The host CPU's model string (/proc/cpuinfo), for every CPU-baseline record."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
 
 def cpu_sample(seed: int, batch: int):
     """Host-resident C2-shaped layer: the first `batch` sequences of the C2 context draw."""
@@ -225,6 +239,7 @@ def cpu_config_baselines(seed: int, threads: int, budget_s: float = 4.0) -> dict
                            f"prefill, one layer timed ({n1}/{n2} runs), x28 layers"}
     for v in res.values():
         v["cores"] = threads
+        v["cpu_model"] = cpu_model()
         v["kind"] = "port"
     return res
 
@@ -279,9 +294,12 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16 KV, C2 shapes)", "impl": "reference",
         "config": {"workload": WORKLOAD, "layers_per_step": 1, "batch": BATCH,
-                   "note": "reference CPU path restated in C++ (Rust reference not buildable here)"},
+                   "note": "reference CPU path restated in C++ (Rust reference not buildable here)",
+                   "gpus_note": "one host process on rank 0 whatever --gpus is: its value does "
+                                "not scale with N, so a GPU/CPU ratio at N > 1 is not a scaling "
+                                "measure"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "cpu_model": cpu_model(), "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -375,6 +393,15 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather(vals):
+        """Every rank's list of floats, indexed by rank (the same list on every rank)."""
+        if world == 1:
+            return [list(vals)]
+        t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=dev)
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [o.tolist() for o in out]
+
     # ---- timed region: K graph replays of the 32-layer decode step ----------------------
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -393,10 +420,19 @@ def run_ours(args):
         torch.cuda.synchronize()
         clocks.mark(w0, time.time())
         barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    own_ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(own_ms)
     ms_per_step = ms / args.steps
     value = kv_bytes_step * args.steps * world / (ms / 1e3) / 1e9
     assert ops.device_status() == 0
+    # Per-rank step time, decode fraction of the measured peak, SM clock and power (each rank's
+    # own sampler over its own GPU), so a slow GPU in a multi-GPU run is named in the record.
+    clk = clocks.summary()
+    own_step = own_ms / args.steps
+    ranks = gather([own_step, bytes_per_layer * NUM_LAYERS / (own_step / 1e3) / 1e9 / hbm_peak,
+                    clk.get("sm_mhz") or 0.0, clk.get("power_w") or 0.0])
+    per_rank = [{"rank": r, "ms_per_step": round(v[0], 4), "hbm_frac": round(v[1], 4),
+                 "sm_mhz": v[2], "power_w": v[3]} for r, v in enumerate(ranks)]
 
     # ---- per-launch duration of the decode kernel (events on the launching stream) -------
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -451,7 +487,8 @@ def run_ours(args):
     # ---- C5 mixed serving step, strong-scaled over the ranks ---------------------------------
     c5 = None
     if not args.no_c5:
-        c5 = run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier)
+        c5 = run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier,
+                    gather)
         torch.cuda.empty_cache()  # return C5's pools before C4 sizes its pool from free memory
 
     # ---- long-context split-K decode (C4) ----------------------------------------------------
@@ -484,12 +521,11 @@ def run_ours(args):
         time_oracle(arrays, threads, 1, 30.0)
         times = time_oracle(arrays, threads, 200, 10.0)
         cpu = {"value": round(nbytes * len(times) / sum(times) / 1e9, 3), "unit": "GB/s",
-               "cores": threads, "kind": "port",
+               "cores": threads, "cpu_model": cpu_model(), "kind": "port",
                "sample": f"{len(times)} x one C2 layer of 16 sequences ({nbytes / 1e6:.0f} MB KV), "
                          "oracle restatement of src/backend/cpu.rs:57-112"}
         cpu_cfg = cpu_config_baselines(args.seed, threads)
 
-    clk = clocks.summary()
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -505,8 +541,14 @@ def run_ours(args):
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "traffic": traffic, "kernel": "paged_decode_kernel<bf16,128,3>",
                          "launch_ms": round(launch_ms, 5),
-                         "isolated_launch_ms": round(dec_avg_ms, 5), "peak_kind": peak_kind,
+                         "frac_uses": "launch_ms: the decode kernel's average launch duration "
+                                      "inside the graph-replayed timed region (step time / 32)",
+                         "isolated_launch_ms": round(dec_avg_ms, 5),
+                         "isolated_frac": round(bytes_per_layer / (dec_avg_ms / 1e3) / 1e9 /
+                                                hbm_peak, 4),
+                         "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": bytes_per_layer},
+            "per_rank": per_rank,
             "gpu_launches": NUM_LAYERS * args.steps,
             "unfused_step_ms": round(unfused_ms, 4),
             "clocks": clk,
@@ -639,7 +681,6 @@ def run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_
     torch.cuda.synchronize()
     reps = 8
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for _ in range(2):
         layer()
     torch.cuda.synchronize()
@@ -649,20 +690,33 @@ def run_prefill(args, torch, ops, make_c3, dev, stream, tc_peak, seed, max_over_
         layer()
     e1.record(stream)
     torch.cuda.synchronize()
+    # The prefill kernel alone: 30 launches, each between its own events on the launching
+    # stream; the median is the kernel time (the suffix K/V are already in the pool).
     ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
-    p0.record(stream)
-    ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
-                      b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len, ws,
-                      out=out)
-    p1.record(stream)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(30)]
+    for p0, p1 in evs:
+        p0.record(stream)
+        ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                          b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len, ws,
+                          out=out)
+        p1.record(stream)
     torch.cuda.synchronize()
+    assert ops.device_status() == 0
     ms = max_over_ranks(e0.elapsed_time(e1)) / reps
-    kernel_ms = p0.elapsed_time(p1)
+    launches = sorted(p0.elapsed_time(p1) for p0, p1 in evs)
+    kernel_ms = max_over_ranks(statistics.median(launches))
     flops = b.flops()
     return {"config": "C3 varlen causal prefill, 16 seqs L~U[128,2048], groups of 4 sharing "
                       "0-50% cached prefixes, Llama-3-8B heads, bf16",
-            "tflops": round(flops * world / (ms / 1e3) / 1e12, 2),
+            "tflops_aggregate": round(flops * world / (ms / 1e3) / 1e12, 2),
+            "tflops_aggregate_note": "reshape_and_cache + prefill per layer, one independent C3 "
+                                     "batch per rank, summed over the ranks",
             "kernel_tflops": round(flops / (kernel_ms / 1e3) / 1e12, 2),
+            "kernel_ms": round(kernel_ms, 5),
+            "kernel_timing": "median of 30 single launches (CUDA events on the launching stream; "
+                             "max over ranks)",
+            "kernel_ms_min_max": [round(launches[0], 5), round(launches[-1], 5)],
             "frac_of_measured_peak": round(flops / (kernel_ms / 1e3) / 1e12 / tc_peak, 4),
             "ms_per_layer": round(ms, 4), "suffix_tokens": int(b.q.shape[0]),
             "flops_per_layer": flops}
@@ -722,96 +776,78 @@ def run_longctx(args, torch, ops, dev, stream, hbm_peak, seed, max_over_ranks, b
     return res
 
 
-def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):
+def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier, gather):
     """C5 mixed serving step: Qwen2-7B heads (Hq=28, Hkv=4, d=128), 28 layers, 512 sequences
     (ctx ~ LogNormal(ln 1024, 0.8) capped at 8192); about 10 % are new prompts of L ~ U[256, 2048]
-    run as prefill, the rest decode one token. The sequences are partitioned longest-first over
-    the ranks (prompts first, then decode sequences where the two-stream step time grows least), so
-    the total work is fixed as N grows (strong scaling). One step = per layer:
+    run as prefill, the rest decode one token. The sequences are partitioned over the ranks
+    (prompts first by kernel work units, then decode sequences where the two-stream step time
+    grows least), so the total work is fixed as N grows (strong scaling). One step = per layer:
     the decode sequences' new K/V write + decode (one fa_paged_decode_append launch) on one
     stream, the prefill sequences' reshape_and_cache and the prefill launch on a second stream
-    (the two sub-batches share no data); each rank owns its
-    own pools. KV values are zero-filled (timing only; the kernels' arithmetic does not depend on
-    the values)."""
-    from flour_b200.workloads import QWEN7B, c5_plan, make_decode, make_prefill, mixed_partition
+    (the two sub-batches share no data); each rank owns its own pools. Pools, queries and new
+    K/V are seeded N(0,1) (only the blocks the tables reference are allocated and filled).
+    Per rank, the decode stream alone and the prefill stream alone are also timed (graphs of one
+    sub-batch), so the record names the limiting kernel on the slowest rank."""
+    from flour_b200.workloads import QWEN7B, c5_plan, make_mixed_step, mixed_partition
     h, L = QWEN7B, 28
     ctx, is_pf, pf_len, cost = c5_plan(args.seed)
     mine = mixed_partition(cost, is_pf, world)[rank]
     dec = [i for i in mine if not is_pf[i]]
     pf = [i for i in mine if is_pf[i]]
-    scale = 1.0 / math.sqrt(h.head_dim)
-    db = make_decode(h, ctx[dec], torch.bfloat16, dev, args.seed + rank, num_layers=L, fill=False)
-    for t in db.k_caches + db.v_caches:
-        t.zero_()
-    B = len(dec)
-    g = torch.Generator(device=dev).manual_seed(args.seed + 11)
-    dq = torch.randn((B, h.num_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
-    dk = torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
-    dv = torch.randn((B, h.num_kv_heads, h.head_dim), device=dev, generator=g).to(torch.bfloat16)
-    dout = torch.empty_like(dq)
-    pb = make_prefill(h, pf_len[pf], np.zeros(len(pf), np.int64), torch.bfloat16, dev,
-                      args.seed + 100 + rank, num_layers=L, fill=False) if pf else None
-    pout = torch.empty_like(pb.q) if pb is not None else None
-    ws_d, ws_p = ops.Workspace(dev), ops.Workspace(dev)
-    ws_d.get(ops.workspace_size(B, h.num_heads, h.num_kv_heads, h.head_dim, db.max_context_len, 1))
-
-    # The decode sequences and the new prompts are independent through every layer, so they run
-    # as two streams (fork and join inside the step): decode CTAs fill the SMs the persistent
-    # prefill kernel leaves idle in its tail, and the other way round.
-    side = torch.cuda.Stream(device=dev)
-
-    def step():
-        main = torch.cuda.current_stream()
-        side.wait_stream(main)
-        for l in range(L):
-            ops.paged_decode_append(dq, db.k_caches[l], db.v_caches[l], dk, dv, db.block_tables,
-                                    db.context_lens, h.n_rep, scale, db.max_context_len, ws_d,
-                                    out=dout)
-        if pb is not None:
-            with torch.cuda.stream(side):
-                for l in range(L):
-                    ops.reshape_and_cache(pb.k_caches[l], pb.v_caches[l], pb.key, pb.value,
-                                          pb.slot_mapping)
-                    ops.paged_prefill(pb.q, pb.k_caches[l], pb.v_caches[l], pb.cu_seqlens_q,
-                                      pb.context_lens, pb.block_tables, h.n_rep, scale,
-                                      pb.max_seqlen_q, pb.max_context_len, ws_p, out=pout)
-        main.wait_stream(side)
+    ms = make_mixed_step(h, ctx[dec], pf_len[pf], torch.bfloat16, dev, args.seed + rank, L)
 
     for _ in range(2):
-        step()
+        ms.run()
     torch.cuda.synchronize()
     assert ops.device_status() == 0
-    # The step as one CUDA graph (84 launches): the host's launch cost stays out of the timing.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    graph.replay()
-    torch.cuda.synchronize()
-    barrier()
-    reps = 5
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
+
+    def timed_graph(fn, reps):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
         graph.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    del graph
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        del graph
+        return e0.elapsed_time(e1) / reps
+
+    # The step as one CUDA graph (decode and prefill streams forked and joined inside it): the
+    # host's launch cost stays out of the timing.
+    own_ms = timed_graph(ms.run, 5)
+    dec_ms = timed_graph(ms.run_decode, 5) if ms.dec is not None else 0.0
+    pf_ms = timed_graph(ms.run_prefill, 5) if ms.pf is not None else 0.0
     assert ops.device_status() == 0
-    own_ms = e0.elapsed_time(e1) / reps
-    ms = max_over_ranks(own_ms)
-    fastest_ms = -max_over_ranks(-own_ms)
+    per_rank = gather([own_ms, dec_ms / L, pf_ms / L])
+    ms_max = max(r[0] for r in per_rank)
+    slow = max(range(world), key=lambda r: per_rank[r][0])
     kvb = h.num_kv_heads * h.head_dim * 2 * 2
     dec_bytes = float(ctx[~is_pf].sum()) * kvb * L
     pf_flops = float((4.0 * h.num_heads * h.head_dim * pf_len[is_pf] * (pf_len[is_pf] + 1) / 2).sum()) * L
     tokens = int((~is_pf).sum() + pf_len[is_pf].sum())
+    del ms
     res = {"config": "C5 mixed serving step: Qwen2-7B heads, 28 layers, 512 seqs (ctx ~ LogNormal"
-                     "(ln 1024, 0.8) <= 8192), ~10 % new prefills L ~ U[256, 2048]; LPT over ranks",
-           "scaling": "strong", "step_ms": round(ms, 4), "fastest_rank_step_ms": round(fastest_ms, 4),
-           "tokens_per_s": round(tokens / (ms / 1e3), 1),
+                     "(ln 1024, 0.8) <= 8192), ~10 % new prefills L ~ U[256, 2048]; partitioned "
+                     "over ranks; seeded N(0,1) pools, queries and new K/V",
+           "scaling": "strong", "step_ms": round(ms_max, 4),
+           "fastest_rank_step_ms": round(min(r[0] for r in per_rank), 4),
+           "tokens_per_s": round(tokens / (ms_max / 1e3), 1),
            "decode_seqs": int((~is_pf).sum()), "prefill_seqs": int(is_pf.sum()),
            "prefill_tokens": int(pf_len[is_pf].sum()),
            "decode_kv_gb_per_step": round(dec_bytes / 1e9, 3),
-           "prefill_tflop_per_step": round(pf_flops / 1e12, 3)}
+           "prefill_tflop_per_step": round(pf_flops / 1e12, 3),
+           "per_rank": [{"rank": r, "step_ms": round(v[0], 4),
+                         "decode_only_ms_per_layer": round(v[1], 5),
+                         "prefill_only_ms_per_layer": round(v[2], 5)}
+                        for r, v in enumerate(per_rank)],
+           "slowest_rank": slow,
+           "slowest_rank_limit": ("prefill" if per_rank[slow][2] >= per_rank[slow][1] else "decode")}
     return res
 
 

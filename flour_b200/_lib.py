@@ -14,6 +14,7 @@ HEADER_PATH = Path(__file__).resolve().parent.parent / "include" / "flour_attn.h
 
 FA_OK, FA_EINVAL, FA_ERANGE, FA_ECUDA, FA_ETIMEOUT, FA_EUNSUPPORTED, FA_EDEVICE = 0, -1, -2, -3, -4, -5, -6
 FA_F32, FA_BF16, FA_F16 = 0, 1, 2
+FA_SCORES_F32, FA_SCORES_REFERENCE = 0, 1
 FA_DEVERR_BLOCK_ID = 0x1
 FA_DEVERR_CONTEXT = 0x2
 FA_DEVERR_SLOT = 0x4
@@ -101,13 +102,14 @@ SIGNATURES = {
     "fa_read_block": (_I32, [_LP, _I32, _P, _P, _P]),
     "fa_paged_attention_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32, _I32]),
     "fa_paged_attention": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
-                                  _I32, _F, _P, _SZ, _P]),
-    "fa_paged_decode": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P, _SZ, _P]),
+                                  _I32, _F, _I32, _P, _SZ, _P]),
+    "fa_paged_decode": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P,
+                               _SZ, _P]),
     "fa_paged_decode_append": (_I32, [_LP, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I32,
-                                      _I32, _I32, _I32, _I32, _F, _P, _SZ, _P]),
+                                      _I32, _I32, _I32, _I32, _F, _I32, _P, _SZ, _P]),
     "fa_paged_decode_noalloc": (_I32, [_LP, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P]),
     "fa_paged_prefill": (_I32, [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
-                                _F, _P, _SZ, _P]),
+                                _F, _I32, _P, _SZ, _P]),
     "fa_qkv_rope_cache": (_I32, [_LP, _WP, _P, _P, _P, _I32, _P, _P]),
     "fa_o_proj_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P]),
     "fa_last_token_logits": (_I32, [_P, _P, _I32, _I32, _P, _F, _P, _I32, _I32, _I32, _P, _P, _P]),
@@ -115,8 +117,8 @@ SIGNATURES = {
     "fa_ipc_free": (_I32, [_P]),
     "fa_ipc_open": (_I32, [_HP, ctypes.POINTER(_P)]),
     "fa_ipc_close": (_I32, [_P]),
-    "fa_paged_decode_tp": (_I32, [_GP, _LP, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _P,
-                                  _SZ, _P]),
+    "fa_paged_decode_tp": (_I32, [_GP, _LP, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32,
+                                  _P, _SZ, _P]),
     "fa_tp_sync": (_I32, [_GP, ctypes.c_uint32, _I32, _I64, _P]),
 }
 

@@ -32,6 +32,7 @@ struct GenericParams {
   int32_t num_blocks;
   int32_t total_q;
   float scale;
+  int32_t ref_scores;  // 1: the reference's dtype rounding of the scores (ref_score)
 };
 
 constexpr int kGenericWarps = 16;
@@ -55,6 +56,7 @@ template <typename T>
 __global__ void __launch_bounds__(kGenericThreads, 1) generic_attn_kernel(const GenericParams p) {
   extern __shared__ float gsm[];
   const int D = p.head_dim, BS = p.block_size;
+  auto score = [&](float dot) { return p.ref_scores ? ref_score<T>(dot, p.scale) : dot * p.scale; };
   float *qs = gsm;                                        // [D]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float *pw = gsm + kGenericMaxDim + size_t(warp) * BS;   // this warp's probabilities [BS]
@@ -146,7 +148,7 @@ __global__ void __launch_bounds__(kGenericThreads, 1) generic_attn_kernel(const 
       float bmax = neg_inf();
 #pragma unroll
       for (int j = 0; j < kSmallRows; ++j) {
-        sc[j] = (j < bn && kv_start + j <= limit) ? sc[j] * p.scale : neg_inf();
+        sc[j] = (j < bn && kv_start + j <= limit) ? score(sc[j]) : neg_inf();
         bmax = fmaxf(bmax, sc[j]);
       }
       const float new_max = fmaxf(m, bmax);
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(kGenericThreads, 1) generic_attn_kernel(const 
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         if (j0 + r < bn) {
-          const float sc = (kv_start + j0 + r > limit) ? neg_inf() : dot[r] * p.scale;
+          const float sc = (kv_start + j0 + r > limit) ? neg_inf() : score(dot[r]);
           if (lane == 0) pw[j0 + r] = sc;
           bmax = fmaxf(bmax, sc);
         }

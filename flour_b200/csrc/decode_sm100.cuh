@@ -74,6 +74,8 @@ struct DecodeParams {
   int32_t max_splits;
   int32_t max_context_len;       // host bound the split plan was made for
   float scale_log2;              // scale * log2(e)
+  float scale;                   // scale as passed (FA_SCORES_REFERENCE rounds it to the dtype)
+  int32_t ref_scores;            // 1: the reference's dtype rounding of the scores (ref_score)
   // Fused append (new_k != nullptr): new_k[b*nk_token + h*nk_head + x] is the new token's key of
   // sequence b, KV head h (same for new_v); it goes to position ctx-1 of k_pool / v_pool.
   const void *new_k;
@@ -270,10 +272,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     }
     // c0:(tok g, head 2t) c1:(g, 2t+1) c2:(g+8, 2t) c3:(g+8, 2t+1)
     const int tok0 = page * kPage + g;
-    const float s0 = tok0 < ctx ? c[0] * sl2 : neg_inf();
-    const float s1 = tok0 < ctx ? c[1] * sl2 : neg_inf();
-    const float s2 = tok0 + 8 < ctx ? c[2] * sl2 : neg_inf();
-    const float s3 = tok0 + 8 < ctx ? c[3] * sl2 : neg_inf();
+    if (p.ref_scores) {  // uniform over the launch
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[e] = ref_score<T>(c[e], p.scale) * kLog2e;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[e] *= sl2;
+    }
+    const float s0 = tok0 < ctx ? c[0] : neg_inf();
+    const float s1 = tok0 < ctx ? c[1] : neg_inf();
+    const float s2 = tok0 + 8 < ctx ? c[2] : neg_inf();
+    const float s3 = tok0 + 8 < ctx ? c[3] : neg_inf();
     float bm0 = fmaxf(s0, s2), bm1 = fmaxf(s1, s3);
 #pragma unroll
     for (int x = 4; x < 32; x <<= 1) {

@@ -20,6 +20,8 @@ __device__ __forceinline__ void report(int bits) { atomicOr(&g_status, bits); }
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
 // ---- element types --------------------------------------------------------------------
 
 template <typename T> struct Elem;
@@ -45,6 +47,36 @@ template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, fl
 template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   __half2 v = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// ---- the reference's score rounding (FA_SCORES_REFERENCE) ---------------------------------
+// src/backend/cpu.rs:84-85 computes `(q.matmul(k^T) * scale).to_dtype(F32)` in the model dtype:
+// the q.k product is rounded to the dtype, multiplied by the scale rounded to the dtype, and the
+// product rounded again. With an f32 accumulator for q.k (the tensor cores' and the oracle's),
+// these helpers reproduce those two roundings. A product of two 16-bit floats is exact in f32,
+// so one hardware multiply rounded to nearest is the reference's single rounding of it. The
+// transform is non-decreasing in `dot` (scale > 0), so it commutes with a row max.
+template <typename T> __device__ __forceinline__ float ref_score(float dot, float scale_t);
+template <> __device__ __forceinline__ float ref_score<float>(float dot, float scale_t) {
+  return dot * scale_t;
+}
+template <> __device__ __forceinline__ float ref_score<__nv_bfloat16>(float dot, float scale_t) {
+  return __bfloat162float(__hmul(__float2bfloat16_rn(dot), __float2bfloat16_rn(scale_t)));
+}
+template <> __device__ __forceinline__ float ref_score<__half>(float dot, float scale_t) {
+  return __half2float(__hmul(__float2half_rn(dot), __float2half_rn(scale_t)));
+}
+// Two scores at once; `scale2` holds the rounded scale twice as a packed 16-bit pair.
+template <typename T> __device__ __forceinline__ float2 ref_score2(float a, float b, uint32_t scale2);
+template <>
+__device__ __forceinline__ float2 ref_score2<__nv_bfloat16>(float a, float b, uint32_t scale2) {
+  const __nv_bfloat162 v = __hmul2(__floats2bfloat162_rn(a, b),
+                                   *reinterpret_cast<const __nv_bfloat162 *>(&scale2));
+  return __bfloat1622float2(v);
+}
+template <> __device__ __forceinline__ float2 ref_score2<__half>(float a, float b, uint32_t scale2) {
+  const __half2 v = __hmul2(__floats2half2_rn(a, b), *reinterpret_cast<const __half2 *>(&scale2));
+  return __half22float2(v);
 }
 
 // ---- misc PTX ---------------------------------------------------------------------------

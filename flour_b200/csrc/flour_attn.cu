@@ -227,8 +227,8 @@ struct AppendArgs {
 
 fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const int32_t *ctx,
                         const int32_t *tables, int max_blocks, int num_seqs, int num_heads,
-                        int n_rep, int max_context_len, float scale, void *ws, size_t ws_bytes,
-                        cudaStream_t stream, const fa_tp_group *tp = nullptr,
+                        int n_rep, int max_context_len, float scale, int score_flow, void *ws,
+                        size_t ws_bytes, cudaStream_t stream, const fa_tp_group *tp = nullptr,
                         bool caller_workspace = true, const AppendArgs *app = nullptr) {
   DecodePlan plan;
   if (!plan_decode(num_seqs, L->num_kv_heads, max_context_len, &plan))
@@ -262,7 +262,9 @@ fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const in
   p.pages_per_split = plan.pages_per_split;
   p.max_splits = plan.max_splits;
   p.max_context_len = max_context_len;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  p.scale_log2 = scale * fa::kLog2e;
+  p.scale = scale;
+  p.ref_scores = score_flow == FA_SCORES_REFERENCE;
   if (tp) {  // head-sharded: every rank's buffer, at this rank's head offset
     p.n_outs = tp->tp;
     p.out_heads = tp->tp * num_heads;
@@ -293,7 +295,8 @@ fa_status launch_decode(const fa_kv_layer *L, const void *q, void *out, const in
 
 fa_status launch_generic(const fa_kv_layer *L, const void *q, void *out, const int32_t *cu,
                          const int32_t *ctx, const int32_t *tables, int max_blocks, int num_seqs,
-                         int num_heads, int n_rep, int total_q, float scale, cudaStream_t stream) {
+                         int num_heads, int n_rep, int total_q, float scale, int score_flow,
+                         cudaStream_t stream) {
   if (L->head_dim > fa::kGenericMaxDim)
     return fail(FA_EUNSUPPORTED, "head_dim %d > %d is not supported", L->head_dim, fa::kGenericMaxDim);
   if (L->block_size > 1024)
@@ -316,6 +319,7 @@ fa_status launch_generic(const fa_kv_layer *L, const void *q, void *out, const i
   p.num_blocks = L->num_blocks;
   p.total_q = total_q;
   p.scale = scale;
+  p.ref_scores = score_flow == FA_SCORES_REFERENCE;
   const size_t smem = fa::generic_smem_floats(L->block_size) * sizeof(float);
   dim3 grid(total_q, num_heads);
   auto launch = [&](auto kern) -> fa_status {
@@ -358,11 +362,11 @@ int sm_count() {
   return cached[dev];
 }
 
-template <typename T>
+template <typename T, bool kRef>
 fa_status launch_prefill_t(const fa::PrefillParams &p, const CUtensorMap &tq, const CUtensorMap &tk,
                            const CUtensorMap &tv, int grid_x, cudaStream_t stream) {
   using S = fa::PrefillSmem;
-  auto kern = fa::paged_prefill_kernel<T>;
+  auto kern = fa::paged_prefill_kernel<T, kRef>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "prefill: set smem attribute: %s", cudaGetErrorString(e));
   kern<<<grid_x, fa::kPfThreads, S::kAlloc, stream>>>(p, tq, tk, tv);
@@ -371,8 +375,8 @@ fa_status launch_prefill_t(const fa::PrefillParams &p, const CUtensorMap &tq, co
 
 fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const int32_t *cu,
                          const int32_t *ctx, const int32_t *tables, int max_blocks, int num_seqs,
-                         int num_heads, int n_rep, int total_q, float scale, void *ws,
-                         size_t ws_bytes, cudaStream_t stream) {
+                         int num_heads, int n_rep, int total_q, float scale, int score_flow,
+                         void *ws, size_t ws_bytes, cudaStream_t stream) {
   if (!ws) return fail(FA_EINVAL, "prefill: workspace is NULL but %zu bytes are needed", kPrefillWorkspace);
   if (ws_bytes < kPrefillWorkspace)
     return fail(FA_ERANGE, "prefill: workspace of %zu bytes, %zu needed", ws_bytes, kPrefillWorkspace);
@@ -387,7 +391,9 @@ fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const i
   p.num_blocks = L->num_blocks;
   p.total_q = total_q;
   p.tq = 128 / n_rep;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  p.scale_log2 = scale * fa::kLog2e;
+  p.scale = scale;
+  const bool ref = score_flow == FA_SCORES_REFERENCE;
   const int64_t rows = int64_t(L->num_blocks) * L->num_kv_heads * L->block_size;
   CUtensorMap tmq, tk, tv;
   if (fa_status s = make_q_map(&tmq, q, total_q, num_heads, n_rep, p.tq, L->dtype); s != FA_OK) return s;
@@ -403,8 +409,12 @@ fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const i
     p.block_tables = tables + size_t(s0) * max_blocks;
     const int64_t items = ((int64_t(total_q) + chunk - 1) / chunk + p.num_seqs) * L->num_kv_heads;
     const int grid = int(std::max<int64_t>(1, std::min<int64_t>(sm_count(), items)));
-    fa_status st = L->dtype == FA_BF16 ? launch_prefill_t<__nv_bfloat16>(p, tmq, tk, tv, grid, stream)
-                                       : launch_prefill_t<__half>(p, tmq, tk, tv, grid, stream);
+    fa_status st =
+        L->dtype == FA_BF16
+            ? (ref ? launch_prefill_t<__nv_bfloat16, true>(p, tmq, tk, tv, grid, stream)
+                   : launch_prefill_t<__nv_bfloat16, false>(p, tmq, tk, tv, grid, stream))
+            : (ref ? launch_prefill_t<__half, true>(p, tmq, tk, tv, grid, stream)
+                   : launch_prefill_t<__half, false>(p, tmq, tk, tv, grid, stream));
     if (st != FA_OK) return st;
   }
   return ok();
@@ -413,7 +423,7 @@ fa_status launch_prefill(const fa_kv_layer *L, const void *q, void *out, const i
 fa_status check_attention_args(const char *who, const fa_kv_layer *L, const void *q, const void *out,
                                const int32_t *ctx, const int32_t *tables, int max_blocks,
                                int num_seqs, int num_heads, int n_rep, int max_context_len,
-                               float scale) {
+                               float scale, int score_flow = FA_SCORES_F32) {
   if (fa_status s = check_layer(L, who); s != FA_OK) return s;
   if (!q || !out || !ctx || !tables) return fail(FA_EINVAL, "%s: NULL query/out/context_lens/block_tables", who);
   if (num_seqs < 0 || max_blocks <= 0) return fail(FA_EINVAL, "%s: num_seqs=%d max_blocks_per_seq=%d", who, num_seqs, max_blocks);
@@ -424,6 +434,9 @@ fa_status check_attention_args(const char *who, const fa_kv_layer *L, const void
     return fail(FA_ERANGE, "%s: max_context_len %d outside [0, %lld]", who, max_context_len,
                 (long long)max_blocks * L->block_size);
   if (!std::isfinite(scale)) return fail(FA_EINVAL, "%s: scale is not finite", who);
+  if (score_flow != FA_SCORES_F32 && score_flow != FA_SCORES_REFERENCE)
+    return fail(FA_EINVAL, "%s: score_flow %d is not FA_SCORES_F32 or FA_SCORES_REFERENCE", who,
+                score_flow);
   return FA_OK;
 }
 
@@ -639,7 +652,7 @@ fa_status launch_qkv(const fa_kv_layer *L, const fa_qkv_weights *w, const void *
 
 extern "C" {
 
-int32_t fa_abi_version(void) { return 1; }
+int32_t fa_abi_version(void) { return 2; }
 
 const char *fa_status_string(int32_t s) {
   switch (s) {
@@ -813,11 +826,12 @@ size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads, in
 fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, void *out,
                           const int32_t *context_lens, const int32_t *block_tables,
                           int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
-                          int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
-                          size_t workspace_bytes, fa_stream_t stream) {
+                          int32_t n_rep, int32_t max_context_len, float scale,
+                          int32_t score_flow, void *workspace, size_t workspace_bytes,
+                          fa_stream_t stream) {
   if (fa_status s = check_attention_args("paged_decode", layer, query, out, context_lens,
                                          block_tables, max_blocks_per_seq, num_seqs, num_heads,
-                                         n_rep, max_context_len, scale);
+                                         n_rep, max_context_len, scale, score_flow);
       s != FA_OK)
     return s;
   if (num_seqs == 0) return ok();
@@ -825,10 +839,10 @@ fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, void *out
   if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "paged_decode: more than 65535 sequences per call");
   if (decode_fast_path(layer, n_rep, query, out))
     return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq,
-                         num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                         num_seqs, num_heads, n_rep, max_context_len, scale, score_flow, workspace,
                          workspace_bytes, stream);
   return launch_generic(layer, query, out, nullptr, context_lens, block_tables, max_blocks_per_seq,
-                        num_seqs, num_heads, n_rep, num_seqs, scale, stream);
+                        num_seqs, num_heads, n_rep, num_seqs, scale, score_flow, stream);
 }
 
 fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *query, const void *key,
@@ -837,12 +851,12 @@ fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *query, co
                                  int64_t value_stride_head, void *out, const int32_t *context_lens,
                                  const int32_t *block_tables, int32_t max_blocks_per_seq,
                                  int32_t num_seqs, int32_t num_heads, int32_t n_rep,
-                                 int32_t max_context_len, float scale, void *workspace,
-                                 size_t workspace_bytes, fa_stream_t stream) {
+                                 int32_t max_context_len, float scale, int32_t score_flow,
+                                 void *workspace, size_t workspace_bytes, fa_stream_t stream) {
   const char *who = "paged_decode_append";
   if (fa_status s = check_attention_args(who, layer, query, out, context_lens, block_tables,
                                          max_blocks_per_seq, num_seqs, num_heads, n_rep,
-                                         max_context_len, scale);
+                                         max_context_len, scale, score_flow);
       s != FA_OK)
     return s;
   if (!key || !value) return fail(FA_EINVAL, "%s: key/value is NULL", who);
@@ -858,7 +872,7 @@ fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *query, co
   const AppendArgs app{key, value, key_stride_token, key_stride_head, value_stride_token,
                        value_stride_head};
   return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq,
-                       num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                       num_seqs, num_heads, n_rep, max_context_len, scale, score_flow, workspace,
                        workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr, true,
                        &app);
 }
@@ -867,11 +881,11 @@ fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *ou
                            const int32_t *cu_seqlens_q, const int32_t *context_lens,
                            const int32_t *block_tables, int32_t max_blocks_per_seq, int32_t num_seqs,
                            int32_t num_heads, int32_t n_rep, int32_t total_q, int32_t max_seqlen_q,
-                           int32_t max_context_len, float scale, void *workspace,
-                           size_t workspace_bytes, fa_stream_t stream) {
+                           int32_t max_context_len, float scale, int32_t score_flow,
+                           void *workspace, size_t workspace_bytes, fa_stream_t stream) {
   if (fa_status s = check_attention_args("paged_prefill", layer, query, out, context_lens,
                                          block_tables, max_blocks_per_seq, num_seqs, num_heads,
-                                         n_rep, max_context_len, scale);
+                                         n_rep, max_context_len, scale, score_flow);
       s != FA_OK)
     return s;
   if (!cu_seqlens_q) return fail(FA_EINVAL, "paged_prefill: cu_seqlens_q is NULL");
@@ -882,9 +896,10 @@ fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, void *ou
   if (prefill_fast_path(layer, n_rep, total_q, scale, query, out))
     return launch_prefill(layer, query, out, cu_seqlens_q, context_lens, block_tables,
                           max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale,
-                          workspace, workspace_bytes, stream);
+                          score_flow, workspace, workspace_bytes, stream);
   return launch_generic(layer, query, out, cu_seqlens_q, context_lens, block_tables,
-                        max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, stream);
+                        max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, scale, score_flow,
+                        stream);
 }
 
 fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query, void *out,
@@ -892,16 +907,17 @@ fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query, void *
                              const int32_t *block_tables, int32_t max_blocks_per_seq,
                              int32_t num_seqs, int32_t num_heads, int32_t n_rep, int32_t total_q,
                              int32_t max_seqlen_q, int32_t max_context_len, float scale,
-                             void *workspace, size_t workspace_bytes, fa_stream_t stream) {
+                             int32_t score_flow, void *workspace, size_t workspace_bytes,
+                             fa_stream_t stream) {
   // Every sequence has exactly one query token when total_q == num_seqs and none has more
   // than one: that is the decode specialisation.
   if (max_seqlen_q == 1 && total_q == num_seqs)
     return fa_paged_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq,
-                           num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
-                           workspace_bytes, stream);
+                           num_seqs, num_heads, n_rep, max_context_len, scale, score_flow,
+                           workspace, workspace_bytes, stream);
   return fa_paged_prefill(layer, query, out, cu_seqlens_q, context_lens, block_tables,
                           max_blocks_per_seq, num_seqs, num_heads, n_rep, total_q, max_seqlen_q,
-                          max_context_len, scale, workspace, workspace_bytes, stream);
+                          max_context_len, scale, score_flow, workspace, workspace_bytes, stream);
 }
 
 fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, void *out,
@@ -919,7 +935,8 @@ fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, v
   if (num_seqs > 65535) return fail(FA_EUNSUPPORTED, "paged_decode_noalloc: more than 65535 sequences per call");
   if (!decode_fast_path(layer, n_rep, query, out))  // the generic kernel uses no scratch
     return launch_generic(layer, query, out, nullptr, context_lens, block_tables,
-                          max_blocks_per_seq, num_seqs, num_heads, n_rep, num_seqs, scale, stream);
+                          max_blocks_per_seq, num_seqs, num_heads, n_rep, num_seqs, scale,
+                          FA_SCORES_F32, stream);
   DecodePlan plan;
   if (!plan_decode(num_seqs, layer->num_kv_heads, max_context_len, &plan))
     return fail(FA_EUNSUPPORTED, "paged_decode_noalloc: context of %d tokens needs more than %d splits",
@@ -941,7 +958,7 @@ fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, v
     if (e != cudaSuccess) return fail(FA_ECUDA, "paged_decode_noalloc: %s", cudaGetErrorString(e));
   }
   return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq, num_seqs,
-                       num_heads, n_rep, max_context_len, scale, scratch,
+                       num_heads, n_rep, max_context_len, scale, FA_SCORES_F32, scratch,
                        FA_NOALLOC_DECODE_SCRATCH_BYTES, stream, nullptr, false);
 }
 
@@ -1111,8 +1128,9 @@ static fa_status check_tp_group(const fa_tp_group *g, const char *who) {
 fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer, const void *query,
                              const int32_t *context_lens, const int32_t *block_tables,
                              int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
-                             int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
-                             size_t workspace_bytes, fa_stream_t stream) {
+                             int32_t n_rep, int32_t max_context_len, float scale,
+                             int32_t score_flow, void *workspace, size_t workspace_bytes,
+                             fa_stream_t stream) {
   const char *who = "paged_decode_tp";
   if (fa_status s = check_tp_group(group, who); s != FA_OK) return s;
   for (int r = 0; r < group->tp; ++r)
@@ -1120,7 +1138,7 @@ fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer,
       return fail(FA_EINVAL, "%s: out[%d] is NULL or not 16-byte aligned", who, r);
   if (fa_status s = check_attention_args(who, layer, query, group->out[group->rank], context_lens,
                                          block_tables, max_blocks_per_seq, num_seqs, num_heads,
-                                         n_rep, max_context_len, scale);
+                                         n_rep, max_context_len, scale, score_flow);
       s != FA_OK)
     return s;
   if (num_seqs == 0) return ok();
@@ -1131,7 +1149,7 @@ fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer *layer,
                 "%s: needs a 16-bit pool, block_size 16, head_dim 64/128, n_rep <= 8 and "
                 "16-byte aligned buffers", who);
   return launch_decode(layer, query, nullptr, context_lens, block_tables, max_blocks_per_seq,
-                       num_seqs, num_heads, n_rep, max_context_len, scale, workspace,
+                       num_seqs, num_heads, n_rep, max_context_len, scale, score_flow, workspace,
                        workspace_bytes, reinterpret_cast<cudaStream_t>(stream), group);
 }
 

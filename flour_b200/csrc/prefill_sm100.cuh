@@ -58,6 +58,7 @@ struct PrefillParams {
   int32_t total_q;
   int32_t tq;                    // query tokens per Q tile (128 / n_rep)
   float scale_log2;              // scale * log2(e), > 0
+  float scale;                   // scale as passed (the reference flow rounds it to the dtype)
 };
 
 constexpr int kPfSoftmaxWarps = 16;         // 2 Q tiles x 2 column halves x 4 row quadrants
@@ -114,7 +115,8 @@ __device__ __forceinline__ bool pair_all(int id, bool v) {
   return r != 0;
 }
 
-template <typename T>
+// kRef: the reference's dtype rounding of the scores (ref_score, FA_SCORES_REFERENCE).
+template <typename T, bool kRef>
 __global__ void __launch_bounds__(kPfThreads, 1)
     paged_prefill_kernel(const __grid_constant__ PrefillParams p,
                          const __grid_constant__ CUtensorMap tm_q,
@@ -431,6 +433,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float *xch_own = xch + (X * 2 + hh) * 128 + r;
     const float *xch_mate = xch + (X * 2 + (hh ^ 1)) * 128 + r;
     const float sl2 = p.scale_log2;
+    const uint32_t scale2 = pack2<T>(p.scale, p.scale);  // the scale rounded to T, twice
     const bool row_used = r < p.tq * p.n_rep;
     int g = 0, v = 0;
     bool ok = true;
@@ -486,7 +489,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                     fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
         *xch_own = mx_half;
         pair_sync(pair_bar);
-        const float mt = fmaxf(mx_half, *xch_mate) * sl2;  // both halves: the same row max
+        // Both halves: the same row max, in log2 units (the rounding of the reference flow is
+        // monotone, so the max of the rounded scores is the rounded max).
+        const float mx = fmaxf(mx_half, *xch_mate);
+        const float mt = kRef ? ref_score<T>(mx, p.scale) * kLog2e : mx * sl2;
         float factor = 1.f;
         bool rescale = false;
         if (i == 0) {
@@ -505,8 +511,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, neg_m));
-            const float b = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, neg_m));
+            float a, b;
+            if constexpr (kRef) {
+              const float2 t = ref_score2<T>(__uint_as_float(sr[c][2 * e]),
+                                             __uint_as_float(sr[c][2 * e + 1]), scale2);
+              a = ex2(fmaf(t.x, kLog2e, neg_m));
+              b = ex2(fmaf(t.y, kLog2e, neg_m));
+            } else {
+              a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, neg_m));
+              b = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, neg_m));
+            }
             rsp[(2 * e) & 7] += a;
             rsp[(2 * e + 1) & 7] += b;
             pk[e] = pack2<T>(a, b);

@@ -512,7 +512,7 @@ AttentionScratch::~AttentionScratch() {
 
 void paged_attention(const DeviceTensor &q, const SequenceBlocks &blocks, int32_t n_rep,
                             double scale, DeviceTensor &out, AttentionScratch &scratch,
-                            fa_stream_t stream) {
+                            fa_stream_t stream, int32_t score_flow) {
   if (q.rank() != 3 || out.shape != q.shape)
     throw Error("paged_attention: q and out must be [q_len, num_heads, head_dim], got q=" +
                 q.dims() + " out=" + out.dims());
@@ -551,7 +551,8 @@ void paged_attention(const DeviceTensor &q, const SequenceBlocks &blocks, int32_
   }
   check(fa_paged_attention(&blocks.layer, q.data, out.data, scratch.tables, scratch.tables + 2,
                            scratch.tables + 3, nb, 1, num_heads, n_rep, q_len, q_len, kv_len,
-                           float(scale), scratch.workspace, scratch.workspace_bytes, stream),
+                           float(scale), score_flow, scratch.workspace, scratch.workspace_bytes,
+                           stream),
         "paged_attention");
 }
 

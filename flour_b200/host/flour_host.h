@@ -267,9 +267,11 @@ struct AttentionScratch {
   int32_t *tables = nullptr;   // [2 + 1 + max_blocks]: cu_seqlens, context_len, block table
   size_t tables_cap = 0;
 };
+// score_flow: FA_SCORES_F32 (default) or FA_SCORES_REFERENCE (the reference's bf16/f16 score
+// rounding of cpu.rs:84-85).
 void paged_attention(const DeviceTensor &q, const SequenceBlocks &blocks, int32_t n_rep,
                      double scale, DeviceTensor &out, AttentionScratch &scratch,
-                     fa_stream_t stream = nullptr);
+                     fa_stream_t stream = nullptr, int32_t score_flow = FA_SCORES_F32);
 
 // ---- batched metadata (new) ------------------------------------------------------------------
 // Sequence i contributes q_lens[i] new tokens (its last q_lens[i] positions) and its table's

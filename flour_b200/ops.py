@@ -123,8 +123,10 @@ def _ws_args(ws: Workspace | None, need: int):
 
 def paged_decode(query, k_cache, v_cache, block_tables, context_lens, n_rep: int, scale: float,
                  max_context_len: int, workspace: Workspace | None = None, out=None,
-                 stream=None):
-    """One query token per sequence: query [B, Hq, d] -> out [B, Hq, d]."""
+                 stream=None, score_flow: int = _lib.FA_SCORES_F32):
+    """One query token per sequence: query [B, Hq, d] -> out [B, Hq, d]. `score_flow`:
+    FA_SCORES_F32 (default) or FA_SCORES_REFERENCE (the reference's bf16/f16 score rounding,
+    src/backend/cpu.rs:84-85)."""
     layer = layer_desc(k_cache, v_cache)
     query = query.contiguous()
     out = torch.empty_like(query) if out is None else out
@@ -133,14 +135,15 @@ def paged_decode(query, k_cache, v_cache, block_tables, context_lens, n_rep: int
     need = workspace_size(B, hq, k_cache.shape[1], d, max_context_len, 1)
     wp, wn = _ws_args(workspace, need)
     check(lib().fa_paged_decode(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cl), _ptr(bt),
-                                bt.shape[1], B, hq, n_rep, max_context_len, scale, wp, wn,
-                                _stream(stream)), "paged_decode")
+                                bt.shape[1], B, hq, n_rep, max_context_len, scale, score_flow,
+                                wp, wn, _stream(stream)), "paged_decode")
     return out
 
 
 def paged_decode_append(query, k_cache, v_cache, key, value, block_tables, context_lens,
                         n_rep: int, scale: float, max_context_len: int,
-                        workspace: Workspace | None = None, out=None, stream=None):
+                        workspace: Workspace | None = None, out=None, stream=None,
+                        score_flow: int = _lib.FA_SCORES_F32):
     """Write each sequence's new token (key/value [B, kv_heads, d], any token/head strides,
     unit stride on d) at position context_lens[b]-1, then decode query [B, Hq, d] over the whole
     context, in one launch: reshape_and_cache + paged_decode of a decode step."""
@@ -158,8 +161,9 @@ def paged_decode_append(query, k_cache, v_cache, key, value, block_tables, conte
     check(lib().fa_paged_decode_append(ctypes.byref(layer), _ptr(query), _ptr(key), _ptr(value),
                                        key.stride(0), key.stride(1), value.stride(0),
                                        value.stride(1), _ptr(out), _ptr(cl), _ptr(bt),
-                                       bt.shape[1], B, hq, n_rep, max_context_len, scale, wp, wn,
-                                       _stream(stream)), "paged_decode_append")
+                                       bt.shape[1], B, hq, n_rep, max_context_len, scale,
+                                       score_flow, wp, wn, _stream(stream)),
+          "paged_decode_append")
     return out
 
 
@@ -180,7 +184,8 @@ def paged_decode_noalloc(query, k_cache, v_cache, block_tables, context_lens, n_
 
 def paged_prefill(query, k_cache, v_cache, cu_seqlens_q, context_lens, block_tables, n_rep: int,
                   scale: float, max_seqlen_q: int, max_context_len: int,
-                  workspace: Workspace | None = None, out=None, stream=None):
+                  workspace: Workspace | None = None, out=None, stream=None,
+                  score_flow: int = _lib.FA_SCORES_F32):
     """Varlen causal attention of packed suffix queries [Tq, Hq, d] over prefix+suffix KV."""
     layer = layer_desc(k_cache, v_cache)
     query = query.contiguous()
@@ -193,13 +198,15 @@ def paged_prefill(query, k_cache, v_cache, cu_seqlens_q, context_lens, block_tab
     wp, wn = _ws_args(workspace, need)
     check(lib().fa_paged_prefill(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cu), _ptr(cl),
                                  _ptr(bt), bt.shape[1], S, hq, n_rep, tq, max_seqlen_q,
-                                 max_context_len, scale, wp, wn, _stream(stream)), "paged_prefill")
+                                 max_context_len, scale, score_flow, wp, wn, _stream(stream)),
+          "paged_prefill")
     return out
 
 
 def paged_attention_varlen(query, k_cache, v_cache, cu_seqlens_q, context_lens, block_tables,
                            n_rep: int, scale: float, max_seqlen_q: int, max_context_len: int,
-                           workspace: Workspace | None = None, out=None, stream=None):
+                           workspace: Workspace | None = None, out=None, stream=None,
+                           score_flow: int = _lib.FA_SCORES_F32):
     """The general entry (fa_paged_attention): decode or prefill chosen by the library."""
     layer = layer_desc(k_cache, v_cache)
     query = query.contiguous()
@@ -213,7 +220,7 @@ def paged_attention_varlen(query, k_cache, v_cache, cu_seqlens_q, context_lens, 
     wp, wn = _ws_args(workspace, need)
     check(lib().fa_paged_attention(ctypes.byref(layer), _ptr(query), _ptr(out), _ptr(cu), _ptr(cl),
                                    _ptr(bt), bt.shape[1], S, hq, n_rep, tq, max_seqlen_q,
-                                   max_context_len, scale, wp, wn, _stream(stream)),
+                                   max_context_len, scale, score_flow, wp, wn, _stream(stream)),
           "paged_attention")
     return out
 

@@ -160,7 +160,8 @@ class HeadShardedGroup:
 
     def decode(self, query, k_cache, v_cache, block_tables, context_lens, n_rep: int, scale: float,
                max_context_len: int, workspace=None, wait: bool = True,
-               timeout_ns: int = DEFAULT_TIMEOUT_NS, stream=None) -> torch.Tensor:
+               timeout_ns: int = DEFAULT_TIMEOUT_NS, stream=None,
+               score_flow: int = _lib.FA_SCORES_F32) -> torch.Tensor:
         """Decode this rank's heads (query [B, num_heads/tp, d], k/v_cache holding this rank's KV
         heads) into every rank's output and return the full [B, num_heads, d] output view. With
         `wait` (the default) the sync follows at once; otherwise call ``sync`` before reading the
@@ -184,7 +185,8 @@ class HeadShardedGroup:
         g = self.group_for(epoch)
         check(self._lib.fa_paged_decode_tp(ctypes.byref(g), ctypes.byref(layer), ops._ptr(query),
                                            ops._ptr(cl), ops._ptr(bt), bt.shape[1], B, hq, n_rep,
-                                           max_context_len, scale, wp, wn, ops._stream(stream)),
+                                           max_context_len, scale, score_flow, wp, wn,
+                                           ops._stream(stream)),
               "paged_decode_tp")
         self.epoch = epoch
         self._pending = True

@@ -216,10 +216,10 @@ def make_c3(device, seed: int = 3, dtype=torch.bfloat16, num_layers: int = 1,
 
 
 def make_prefill(heads: Heads, lens, prefix, dtype: torch.dtype, device, seed: int,
-                 num_layers: int = 1, fill: bool = True) -> PrefillBatch:
+                 num_layers: int = 1) -> PrefillBatch:
     """A packed prefill batch: sequence i holds lens[i] tokens, the first prefix[i] of them
-    already cached; every sequence owns private, randomly placed blocks of one pool. With
-    fill=False the pools, queries and new K/V are zero-filled instead of random (timing runs)."""
+    already cached; every sequence owns private, randomly placed blocks of one pool. Pools,
+    queries and new K/V are seeded N(0,1)."""
     rng = np.random.default_rng(seed)
     bs = heads.block_size
     lens = np.asarray(lens, dtype=np.int64)
@@ -240,8 +240,7 @@ def make_prefill(heads: Heads, lens, prefix, dtype: torch.dtype, device, seed: i
                            ) if len(lens) else np.zeros(0, np.int64)
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
-    make = (lambda shape: _randn(shape, dtype, device, gen)) if fill else \
-        (lambda shape: torch.zeros(shape, dtype=dtype, device=device))
+    make = lambda shape: _randn(shape, dtype, device, gen)  # noqa: E731
     shape = (total, heads.num_kv_heads, bs, heads.head_dim)
     kc = [make(shape) for _ in range(num_layers)]
     vc = [make(shape) for _ in range(num_layers)]
@@ -324,6 +323,85 @@ def lpt_partition(costs, parts: int) -> list[list[int]]:
         bins[j].append(int(i))
         loads[j] += float(costs[i])
     return [sorted(b) for b in bins]
+
+
+@dataclass
+class MixedStep:
+    """One C5 serving step on one GPU: the decode sequences (one new token each, written and
+    attended in one fa_paged_decode_append launch per layer) on the caller's stream and the new
+    prompts (fa_reshape_and_cache of their K/V, then fa_paged_prefill, per layer) on a side
+    stream, forked and joined inside ``run``. The two sub-batches share no data through any
+    layer, so decode CTAs fill the SMs the persistent prefill kernel leaves idle in its tail and
+    the other way round. Every layer writes the same output buffers (``dout``, ``pout``)."""
+    heads: Heads
+    num_layers: int
+    dec: DecodeBatch | None
+    dk: torch.Tensor | None          # [B, Hkv, d] the decode sequences' new K and V
+    dv: torch.Tensor | None
+    dout: torch.Tensor | None        # [B, Hq, d]
+    pf: PrefillBatch | None
+    pout: torch.Tensor | None        # [Tq, Hq, d]
+    ws_dec: object = None
+    ws_pf: object = None
+    side: object = None
+    score_flow: int = 0              # FA_SCORES_F32 or FA_SCORES_REFERENCE
+
+    def run_decode(self):
+        from . import ops
+        h, b = self.heads, self.dec
+        scale = 1.0 / float(np.sqrt(h.head_dim))
+        for l in range(self.num_layers):
+            ops.paged_decode_append(b.q, b.k_caches[l], b.v_caches[l], self.dk, self.dv,
+                                    b.block_tables, b.context_lens, h.n_rep, scale,
+                                    b.max_context_len, self.ws_dec, out=self.dout,
+                                    score_flow=self.score_flow)
+
+    def run_prefill(self):
+        from . import ops
+        h, b = self.heads, self.pf
+        scale = 1.0 / float(np.sqrt(h.head_dim))
+        for l in range(self.num_layers):
+            ops.reshape_and_cache(b.k_caches[l], b.v_caches[l], b.key, b.value, b.slot_mapping)
+            ops.paged_prefill(b.q, b.k_caches[l], b.v_caches[l], b.cu_seqlens_q, b.context_lens,
+                              b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len,
+                              self.ws_pf, out=self.pout, score_flow=self.score_flow)
+
+    def run(self):
+        main = torch.cuda.current_stream()
+        self.side.wait_stream(main)
+        if self.dec is not None:
+            self.run_decode()
+        if self.pf is not None:
+            with torch.cuda.stream(self.side):
+                self.run_prefill()
+        main.wait_stream(self.side)
+
+
+def make_mixed_step(heads: Heads, dec_ctx, pf_len, dtype: torch.dtype, device, seed: int,
+                    num_layers: int) -> MixedStep:
+    """Seeded N(0,1) pools (only the blocks the tables reference exist), queries and new K/V for
+    a mixed step: decode sequences with contexts `dec_ctx` (the new token included) and new
+    prompts of lengths `pf_len` with no cached prefix."""
+    from . import ops
+    dec_ctx = np.asarray(dec_ctx, dtype=np.int64)
+    pf_len = np.asarray(pf_len, dtype=np.int64)
+    dec = dk = dv = dout = pf = pout = None
+    ws_dec = ops.Workspace(device)
+    if len(dec_ctx):
+        dec = make_decode(heads, dec_ctx, dtype, device, seed, num_layers=num_layers)
+        g = torch.Generator(device=device).manual_seed(seed + 11)
+        B = dec.num_seqs
+        dk = _randn((B, heads.num_kv_heads, heads.head_dim), dtype, device, g)
+        dv = _randn((B, heads.num_kv_heads, heads.head_dim), dtype, device, g)
+        dout = torch.empty_like(dec.q)
+        ws_dec.get(ops.workspace_size(B, heads.num_heads, heads.num_kv_heads, heads.head_dim,
+                                      dec.max_context_len, 1))
+    if len(pf_len):
+        pf = make_prefill(heads, pf_len, np.zeros(len(pf_len), np.int64), dtype, device,
+                          seed + 100, num_layers=num_layers)
+        pout = torch.empty_like(pf.q)
+    return MixedStep(heads, num_layers, dec, dk, dv, dout, pf, pout, ws_dec, ops.Workspace(device),
+                     torch.cuda.Stream(device=device))
 
 
 def to_numpy(t: torch.Tensor) -> np.ndarray:

@@ -75,6 +75,18 @@ typedef enum fa_dtype { FA_F32 = 0, FA_BF16 = 1, FA_F16 = 2 } fa_dtype;
 #define FA_DEVERR_POSITION 0x40  /* RoPE position outside [0, max_position) */
 #define FA_DEVERR_LAUNCH 0x80    /* a kernel refused a launch shape it does not support */
 
+/* How attention scores are formed before the softmax (the `score_flow` argument).
+ *   FA_SCORES_F32        q.k accumulated in f32 and multiplied by scale in f32 (the default:
+ *                        the most accurate, and the fastest prefill).
+ *   FA_SCORES_REFERENCE  the reference's dtype flow for bf16/f16 pools, src/backend/cpu.rs:84-85
+ *                        `(q.matmul(k^T) * scale).to_dtype(F32)`: q.k (f32 accumulation) rounded
+ *                        to the pool dtype, multiplied by scale rounded to the pool dtype, the
+ *                        product rounded again, then used in f32. Outputs then track the
+ *                        reference CPU backend's own rounding; for f32 pools both flows are
+ *                        identical. The softmax, the f32 accumulation of P.V and the output
+ *                        rounding are the same in both flows. */
+typedef enum fa_score_flow { FA_SCORES_F32 = 0, FA_SCORES_REFERENCE = 1 } fa_score_flow;
+
 /* One layer of the paged KV pool. */
 typedef struct fa_kv_layer {
   void *k_cache;          /* device, [num_blocks, num_kv_heads, block_size, head_dim] */
@@ -161,7 +173,7 @@ FA_API fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query,
                              const int32_t *block_tables, int32_t max_blocks_per_seq,
                              int32_t num_seqs, int32_t num_heads, int32_t n_rep,
                              int32_t total_q, int32_t max_seqlen_q, int32_t max_context_len,
-                             float scale, void *workspace, size_t workspace_bytes,
+                             float scale, int32_t score_flow, void *workspace, size_t workspace_bytes,
                              fa_stream_t stream);
 
 /* Decode specialisation (one query token per sequence): query/out [num_seqs, num_heads, d].
@@ -169,7 +181,7 @@ FA_API fa_status fa_paged_attention(const fa_kv_layer *layer, const void *query,
 FA_API fa_status fa_paged_decode(const fa_kv_layer *layer, const void *query, void *out,
                           const int32_t *context_lens, const int32_t *block_tables,
                           int32_t max_blocks_per_seq, int32_t num_seqs, int32_t num_heads,
-                          int32_t n_rep, int32_t max_context_len, float scale, void *workspace,
+                          int32_t n_rep, int32_t max_context_len, float scale, int32_t score_flow, void *workspace,
                           size_t workspace_bytes, fa_stream_t stream);
 
 /* One decode step of the reference's attention in one launch: Cache::write_kv of the new token
@@ -192,7 +204,7 @@ FA_API fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *qu
                                         void *out, const int32_t *context_lens,
                                         const int32_t *block_tables, int32_t max_blocks_per_seq,
                                         int32_t num_seqs, int32_t num_heads, int32_t n_rep,
-                                        int32_t max_context_len, float scale, void *workspace,
+                                        int32_t max_context_len, float scale, int32_t score_flow, void *workspace,
                                         size_t workspace_bytes, fa_stream_t stream);
 
 /* Decode without a caller-provided workspace. No counterpart in the reference: the reference's
@@ -203,7 +215,7 @@ FA_API fa_status fa_paged_decode_append(const fa_kv_layer *layer, const void *qu
  * its own. For them this variant takes its split-K scratch from a fixed buffer inside the
  * library (FA_NOALLOC_DECODE_SCRATCH_BYTES; every GPU that loads the library holds it until the
  * process exits) and calls no allocating routine. Same arguments and results as
- * fa_paged_decode minus the workspace.
+ * fa_paged_decode with score_flow FA_SCORES_F32, minus the workspace.
  *   - Requests whose split-K scratch would exceed FA_NOALLOC_DECODE_SCRATCH_BYTES are rejected
  *     with FA_ERANGE (use fa_paged_decode with a workspace for those). The test is exact: a call
  *     is accepted when fa_paged_attention_workspace_size(num_seqs, num_heads, num_kv_heads,
@@ -229,7 +241,7 @@ FA_API fa_status fa_paged_prefill(const fa_kv_layer *layer, const void *query, v
                            const int32_t *cu_seqlens_q, const int32_t *context_lens,
                            const int32_t *block_tables, int32_t max_blocks_per_seq,
                            int32_t num_seqs, int32_t num_heads, int32_t n_rep, int32_t total_q,
-                           int32_t max_seqlen_q, int32_t max_context_len, float scale,
+                           int32_t max_seqlen_q, int32_t max_context_len, float scale, int32_t score_flow,
                            void *workspace, size_t workspace_bytes, fa_stream_t stream);
 
 /* ---- the steps either side of attention (CausalSelfAttention::forward) ----------------- */
@@ -347,7 +359,7 @@ FA_API fa_status fa_paged_decode_tp(const fa_tp_group *group, const fa_kv_layer 
                                     const void *query, const int32_t *context_lens,
                                     const int32_t *block_tables, int32_t max_blocks_per_seq,
                                     int32_t num_seqs, int32_t num_heads, int32_t n_rep,
-                                    int32_t max_context_len, float scale, void *workspace,
+                                    int32_t max_context_len, float scale, int32_t score_flow, void *workspace,
                                     size_t workspace_bytes, fa_stream_t stream);
 
 /* FA_TP_PUBLISH: store the epoch into every rank's flag slot [group->rank]; FA_TP_WAIT: make

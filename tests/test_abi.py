@@ -34,7 +34,7 @@ def test_library_is_built_for_sm100a():
 
 def test_status_strings():
     L = lib()
-    assert L.fa_abi_version() == 1
+    assert L.fa_abi_version() == 2
     assert L.fa_status_string(0) == b"ok"
     assert L.fa_status_string(-1) == b"invalid argument"
     assert L.fa_status_string(-6) == b"kernel reported bad device data"
@@ -50,15 +50,18 @@ def test_host_validation_rejects_before_launch():
     ly = layer()
     fake = P(0x10000)
     # NULL layer
-    assert L.fa_paged_decode(None, fake, fake, fake, fake, 4, 1, 4, 2, 16, 0.1, None, 0, None) == _lib.FA_EINVAL
+    assert L.fa_paged_decode(None, fake, fake, fake, fake, 4, 1, 4, 2, 16, 0.1, 0, None, 0, None) == _lib.FA_EINVAL
     assert b"layer is NULL" in L.fa_last_error_message()
     # num_heads != n_rep * kv_heads (repeat_kv contract, cpu.rs:78-79)
-    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 5, 2, 16, 0.1, None, 0, None) == _lib.FA_EINVAL
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 5, 2, 16, 0.1, 0, None, 0, None) == _lib.FA_EINVAL
     assert b"n_rep" in L.fa_last_error_message()
     # context longer than the table can hold
-    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 65, 0.1, None, 0, None) == _lib.FA_ERANGE
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 65, 0.1, 0, None, 0, None) == _lib.FA_ERANGE
     # non-finite scale
-    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 16, float("nan"), None, 0, None) == _lib.FA_EINVAL
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 16, float("nan"), 0, None, 0, None) == _lib.FA_EINVAL
+    # unknown score flow
+    assert L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 4, 1, 4, 2, 16, 0.1, 2, None, 0, None) == _lib.FA_EINVAL
+    assert b"score_flow" in L.fa_last_error_message()
     # bad dtype
     bad = layer(dt=7)
     assert L.fa_reshape_and_cache(ctypes.byref(bad), fake, fake, 128, 64, 128, 64, fake, 3, None) == _lib.FA_EINVAL
@@ -70,7 +73,7 @@ def test_host_validation_rejects_before_launch():
     two = (FaKvLayer * 2)(layer(), layer(d=128))
     assert L.fa_copy_blocks(two, 2, fake, 1, None) == _lib.FA_EINVAL
     # prefill: query longer than the context
-    assert L.fa_paged_prefill(ctypes.byref(ly), fake, fake, fake, fake, fake, 4, 1, 4, 2, 8, 8, 4, 0.1, None, 0, None) == _lib.FA_ERANGE
+    assert L.fa_paged_prefill(ctypes.byref(ly), fake, fake, fake, fake, fake, 4, 1, 4, 2, 8, 8, 4, 0.1, 0, None, 0, None) == _lib.FA_ERANGE
     # empty work is a no-op success
     assert L.fa_reshape_and_cache(ctypes.byref(ly), fake, fake, 128, 64, 128, 64, fake, 0, None) == _lib.FA_OK
     assert L.fa_copy_blocks(ctypes.byref(ly), 1, fake, 0, None) == _lib.FA_OK
@@ -95,6 +98,6 @@ def test_decode_workspace_too_small_is_rejected_without_launch():
     need = L.fa_paged_attention_workspace_size(64, 32, 8, 128, 4096, 1)
     assert need > 0
     st = L.fa_paged_decode(ctypes.byref(ly), fake, fake, fake, fake, 256, 64, 32, 4, 4096, 0.1,
-                           ctypes.c_void_p(0x100000), need - 1, None)
+                           0, ctypes.c_void_p(0x100000), need - 1, None)
     assert st == _lib.FA_ERANGE
     assert b"workspace" in L.fa_last_error_message()

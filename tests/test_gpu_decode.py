@@ -23,12 +23,19 @@ TOL_F32 = 1e-5
 TOL_BF16 = 2e-2
 
 
-def run_decode(batch, ws=None, max_context_len=None):
+def run_decode(batch, ws=None, max_context_len=None, score_flow=_lib.FA_SCORES_F32):
     h = batch.heads
     ws = ws or ops.Workspace(batch.q.device)
     return ops.paged_decode(batch.q, batch.k_caches[0], batch.v_caches[0], batch.block_tables,
                             batch.context_lens, h.n_rep, 1.0 / math.sqrt(h.head_dim),
-                            max_context_len or batch.max_context_len, ws)
+                            max_context_len or batch.max_context_len, ws, score_flow=score_flow)
+
+
+def check_both_flows(batch, tol):
+    """The default flow against f32-score oracle (score_mode 0), and FA_SCORES_REFERENCE
+    against the reference's dtype flow (score_mode 1, cpu.rs:84-85)."""
+    check(batch, run_decode(batch), tol, score_modes=(0,))
+    check(batch, run_decode(batch, score_flow=_lib.FA_SCORES_REFERENCE), tol, score_modes=(1,))
 
 
 def check(batch, out, tol, score_modes=(0,)):
@@ -52,25 +59,32 @@ def test_c1_qwen05_f32(device):
 @pytest.mark.parametrize("seed", [2, 3])
 def test_c2_llama8b_bf16(device, seed):
     b = make_decode(LLAMA8B, c2_contexts(seed, batch=8), torch.bfloat16, device, seed)
-    check(b, run_decode(b), TOL_BF16, score_modes=(0, 1))
+    check_both_flows(b, TOL_BF16)
 
 
 def test_c2_full_batch_against_oracle(device):
     # All 64 sequences of the benchmark configuration (one layer).
     b = make_decode(LLAMA8B, c2_contexts(1234), torch.bfloat16, device, 1234)
-    check(b, run_decode(b), TOL_BF16)
+    check_both_flows(b, TOL_BF16)
 
 
 def test_c4_long_context_split_k(device):
     ctx = np.random.default_rng(4).integers(16384, 32769, size=2)
     b = make_decode(LLAMA8B, ctx, torch.bfloat16, device, 4)
-    check(b, run_decode(b), TOL_BF16)
+    check_both_flows(b, TOL_BF16)
 
 
 def test_c5_qwen7b_heads_n_rep_7(device):
     ctx = np.random.default_rng(5).integers(1, 3000, size=12)
     b = make_decode(QWEN7B, ctx, torch.bfloat16, device, 5)
-    check(b, run_decode(b), TOL_BF16)
+    check_both_flows(b, TOL_BF16)
+
+
+def test_c5_decode_context_distribution(device):
+    # C5's decode contexts: LogNormal(ln 1024, 0.8) capped at 8192, Qwen2-7B heads.
+    from flour_b200.workloads import c5_contexts
+    b = make_decode(QWEN7B, c5_contexts(56, 24), torch.bfloat16, device, 56)
+    check_both_flows(b, TOL_BF16)
 
 
 @pytest.mark.parametrize("heads", [QWEN05, Heads(8, 8, 128), Heads(16, 2, 128)])
@@ -83,13 +97,23 @@ def test_other_head_shapes_bf16(device, heads):
 def test_f16_pool(device):
     ctx = np.random.default_rng(7).integers(1, 2500, size=6)
     b = make_decode(LLAMA8B, ctx, torch.float16, device, 7)
-    check(b, run_decode(b), TOL_BF16)
+    check_both_flows(b, TOL_BF16)
 
 
 def test_f32_llama_shapes_generic_path(device):
     ctx = np.random.default_rng(8).integers(1, 700, size=3)
     b = make_decode(LLAMA8B, ctx, torch.float32, device, 8, value_scale=0.125)
     check(b, run_decode(b), TOL_F32)
+    # For f32 pools the reference flow rounds nothing: the same bits as the default flow.
+    assert torch.equal(run_decode(b, score_flow=_lib.FA_SCORES_REFERENCE), run_decode(b))
+
+
+def test_bf16_generic_path_reference_flow(device):
+    # block_size 8 takes the generic kernel; its reference flow against score_mode 1.
+    h = Heads(8, 2, 96, block_size=8)
+    ctx = np.random.default_rng(18).integers(1, 900, size=4)
+    b = make_decode(h, ctx, torch.bfloat16, device, 18)
+    check_both_flows(b, TOL_BF16)
 
 
 @pytest.mark.parametrize("ctx", [[1], [15], [16], [17], [1, 16, 17, 33], [255, 256, 257]])

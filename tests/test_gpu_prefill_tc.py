@@ -50,20 +50,27 @@ def build(device, heads, lens, prefix, seed, dtype=torch.bfloat16):
                         int(suffix.max()), int(lens.max()), total)
 
 
-def run_and_check(b, tol=TOL):
+def run_and_check(b, tol=TOL, flows=(_lib.FA_SCORES_F32,)):
+    """Write the suffix K/V, run the prefill in each score flow and compare with the oracle in
+    the matching mode (FA_SCORES_F32 <-> score_mode 0, f32 scores; FA_SCORES_REFERENCE <->
+    score_mode 1, the reference's bf16 dtype flow of cpu.rs:84-85). Returns the last output."""
     h = b.heads
     scale = 1 / math.sqrt(h.head_dim)
     ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
-    out = ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
-                            b.block_tables, h.n_rep, scale, b.max_seqlen_q, b.max_context_len,
-                            ops.Workspace(b.q.device))
-    torch.cuda.synchronize()
-    assert ops.device_status() == 0
-    want = oracle_attention(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
-                            b.block_tables, h.n_rep, scale)
-    err = max_abs(f32(out), want)
-    assert err <= tol, f"max-abs {err}"
+    for flow in flows:
+        out = ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q,
+                                b.context_lens, b.block_tables, h.n_rep, scale, b.max_seqlen_q,
+                                b.max_context_len, ops.Workspace(b.q.device), score_flow=flow)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        want = oracle_attention(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q, b.context_lens,
+                                b.block_tables, h.n_rep, scale, score_mode=flow)
+        err = max_abs(f32(out), want)
+        assert err <= tol, f"score flow {flow}: max-abs {err}"
     return out
+
+
+BOTH = (_lib.FA_SCORES_F32, _lib.FA_SCORES_REFERENCE)
 
 
 def test_single_sequence_no_prefix(device):
@@ -80,7 +87,8 @@ def test_long_prefix_short_suffix(device):
 
 
 def test_empty_and_one_token_sequences(device):
-    run_and_check(build(device, LLAMA8B, [40, 200, 77, 130, 90], [40, 199, 0, 64, 89], 4))
+    run_and_check(build(device, LLAMA8B, [40, 200, 77, 130, 90], [40, 199, 0, 64, 89], 4),
+                  flows=BOTH)
 
 
 @pytest.mark.parametrize("heads", [Heads(8, 8, 128), Heads(32, 4, 128), QWEN7B, Heads(16, 2, 128)])
@@ -89,11 +97,18 @@ def test_gqa_ratios(device, heads):
 
 
 def test_f16_pool(device):
-    run_and_check(build(device, LLAMA8B, [333, 150], [96, 0], 6, dtype=torch.float16))
+    run_and_check(build(device, LLAMA8B, [333, 150], [96, 0], 6, dtype=torch.float16), flows=BOTH)
 
 
-def test_c3_full_configuration(device):
-    run_and_check(make_c3(device, seed=1003))
+@pytest.mark.parametrize("seed", [1003, 1004, 1005])
+def test_c3_full_configuration(device, seed):
+    run_and_check(make_c3(device, seed=seed), flows=BOTH)
+
+
+def test_c5_prompt_shapes(device):
+    # C5's new prompts: Qwen2-7B heads (n_rep 7), L ~ U[256, 2048], no cached prefix.
+    lens = np.random.default_rng(55).integers(256, 2049, size=5)
+    run_and_check(build(device, QWEN7B, lens, [0] * 5, 55), flows=BOTH)
 
 
 def test_prefill_repeatable(device):

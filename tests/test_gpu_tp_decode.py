@@ -147,7 +147,7 @@ def test_tp_emulated_on_one_gpu(device, tp, heads):
                                               ops._ptr(q), ops._ptr(cl),
                                               ops._ptr(b.block_tables), b.block_tables.shape[1],
                                               b.num_seqs, q.shape[1], h.n_rep, b.max_context_len,
-                                              scale, wp, wn, stream), "paged_decode_tp")
+                                              scale, 0, wp, wn, stream), "paged_decode_tp")
             _lib.check(lib.fa_tp_sync(ctypes.byref(groups[rank]), epoch, _lib.FA_TP_PUBLISH, 0,
                                       stream), "tp_sync publish")
         for rank in range(tp):
@@ -210,7 +210,7 @@ def test_tp_rejects_bad_groups_and_unsynced_decodes(device):
     layer = ops.layer_desc(kc, vc)
     st = lib.fa_paged_decode_tp(ctypes.byref(g), ctypes.byref(layer), ops._ptr(q),
                                 ops._ptr(b.context_lens), ops._ptr(b.block_tables), 4, 1,
-                                q.shape[1], h.n_rep, 64, 0.1, None, 0, None)
+                                q.shape[1], h.n_rep, 64, 0.1, 0, None, 0, None)
     assert st == _lib.FA_EINVAL
     assert b"out[1]" in lib.fa_last_error_message()
     grp = HeadShardedGroup(1, 0, 1, h.num_heads, h.head_dim, torch.bfloat16, lambda x: [x], device)
