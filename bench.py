@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--no-c5", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="skip the head-sharded decode (N > 1)")
+    ap.add_argument("--no-bundle", action="store_true", help="skip the FLKV export measurement")
     return ap.parse_args()
 
 
@@ -509,6 +510,9 @@ def run_ours(args):
         proj = run_projections(torch, ops, dev, stream, tc_peak, hbm_peak, seed, max_over_ranks,
                                barrier)
 
+    bundle = run_bundle(torch, ops, batch, dev, stream, hbm_peak, seed) \
+        if not args.no_bundle else None
+
     c1 = run_c1(torch, ops, dev, stream) if world == 1 else None
 
     # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------------
@@ -579,6 +583,8 @@ def run_ours(args):
             line["cpu_baseline_configs"] = cpu_cfg
         if tp:
             line["tp_decode"] = tp
+        if bundle:
+            line["bundle_export"] = bundle
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
@@ -849,6 +855,74 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier, 
            "slowest_rank": slow,
            "slowest_rank_limit": ("prefill" if per_rank[slow][2] >= per_rank[slow][1] else "decode")}
     return res
+
+
+def run_bundle(torch, ops, batch, dev, stream, hbm_peak, seed):
+    """FLKV prefix export (KvCache::export_prefix_bundle, cache.rs:166-228; payload order
+    bundle.rs:15-22) of a 2048-token prefix of the C2 pools: 128 blocks x 32 layers (268 MB).
+    `kernel`: the one-launch gather into a device payload (bytes read + written over its time);
+    `to_host`: gather + one D2H copy into pinned memory; `per_block_route`: the same bytes as
+    2 x blocks x layers cudaMemcpyAsync (fa_read_block) into pinned memory."""
+    nb = batch.k_caches[0].shape[0]
+    ids = torch.from_numpy(np.random.default_rng(seed + 9).permutation(nb)[:128].astype(np.int32)
+                           ).to(dev)
+    ks, vs = batch.k_caches, batch.v_caches
+    n = ops.bundle_payload_bytes(ks, vs, 128)
+    payload = torch.empty(n, dtype=torch.uint8, device=dev)
+    host = torch.empty(n, dtype=torch.uint8).pin_memory()
+    for _ in range(3):
+        ops.export_bundle_payload(ks, vs, ids, payload)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(20)]
+    for a, b in evs:
+        a.record(stream)
+        ops.export_bundle_payload(ks, vs, ids, payload)
+        b.record(stream)
+    torch.cuda.synchronize()
+    k_ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+
+    def to_host():
+        ops.export_bundle_payload(ks, vs, ids, payload)
+        host.copy_(payload, non_blocking=True)
+
+    def per_block():
+        piece = n // (128 * len(ks) * 2)
+        ids_h = ids.cpu().tolist()
+        o = 0
+        for b in ids_h:
+            for l in range(len(ks)):
+                kd = host[o:o + piece]
+                vd = host[o + piece:o + 2 * piece]
+                ops.read_block(ks[l], vs[l], b, kd, vd)
+                o += 2 * piece
+
+    def timed(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        t = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t.append(e0.elapsed_time(e1))
+        return statistics.median(t)
+
+    host_ms = timed(to_host)
+    per_ms = timed(per_block, 3)
+    want = host.clone()
+    ok = bool(torch.equal(payload.cpu(), want))
+    assert ops.device_status() == 0
+    return {"config": "FLKV export of a 2048-token prefix: 128 blocks x 32 layers, Llama-3-8B "
+                      "heads, bf16", "payload_bytes": n,
+            "kernel_ms": round(k_ms, 4),
+            "kernel_gbps": round(2 * n / (k_ms / 1e3) / 1e9, 1),
+            "kernel_frac_of_measured_hbm_peak": round(2 * n / (k_ms / 1e3) / 1e9 / hbm_peak, 4),
+            "to_host_ms": round(host_ms, 3), "to_host_gbps": round(n / (host_ms / 1e3) / 1e9, 1),
+            "per_block_route_ms": round(per_ms, 3), "per_block_route_copies": 2 * 128 * len(ks),
+            "payloads_equal": ok}
 
 
 def run_tp_decode(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier):

@@ -97,4 +97,52 @@ __global__ void __launch_bounds__(256) copy_blocks_kernel(const CopyParams p) {
   for (; i < n; i += blockDim.x) d[i] = s[i];
 }
 
+struct BundleParams {
+  char *k[FA_MAX_COPY_LAYERS];
+  char *v[FA_MAX_COPY_LAYERS];
+  const int32_t *block_ids;  // [num_logical]: physical block of each logical block, in order
+  char *payload;             // [num_logical][num_layers][2 (K, V)][block_bytes]
+  int64_t block_bytes;
+  int32_t num_logical;
+  int32_t num_layers;
+  int32_t num_blocks;        // pool size, for the block-id check
+};
+
+// FLKV bundle payload (src/kv_cache/bundle.rs:15-22): for each logical block, for each layer,
+// the K then the V of that block, shape (kv_heads, block_size, head_dim). In the pool layout
+// [num_blocks, kv_heads, block_size, head_dim] each piece is one contiguous run of block_bytes,
+// so the payload is a gather of whole runs (export) or the mirror scatter (import).
+// grid = (2 * num_layers, num_logical): CTA (x, b) moves piece (b, x / 2, x % 2), 4 vectors in
+// flight per thread. Export of a bad block id zero-fills its pieces; import skips them; both
+// set FA_DEVERR_BLOCK_ID.
+template <int V, bool kImport>
+__global__ void __launch_bounds__(256) bundle_payload_kernel(const BundleParams p) {
+  using VT = typename VecT<V>::type;
+  const int l = blockIdx.x >> 1, kv = blockIdx.x & 1, b = blockIdx.y;
+  const int32_t id = p.block_ids[b];
+  const bool bad = uint32_t(id) >= uint32_t(p.num_blocks);
+  if (bad && threadIdx.x == 0 && blockIdx.x == 0) report(FA_DEVERR_BLOCK_ID);
+  VT *piece = reinterpret_cast<VT *>(p.payload + ((int64_t(b) * p.num_layers + l) * 2 + kv) *
+                                                     p.block_bytes);
+  VT *pool = reinterpret_cast<VT *>((kv ? p.v[l] : p.k[l]) + int64_t(bad ? 0 : id) * p.block_bytes);
+  const int64_t n = p.block_bytes / V;
+  if (bad) {
+    if (!kImport)
+      for (int64_t i = threadIdx.x; i < n; i += blockDim.x) piece[i] = VT{};
+    return;
+  }
+  const VT *src = kImport ? piece : pool;
+  VT *dst = kImport ? pool : piece;
+  constexpr int U = 4;
+  int64_t i = threadIdx.x;
+  for (; i + (U - 1) * blockDim.x < n; i += U * blockDim.x) {
+    VT r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) r[u] = src[i + u * blockDim.x];
+#pragma unroll
+    for (int u = 0; u < U; ++u) dst[i + u * blockDim.x] = r[u];
+  }
+  for (; i < n; i += blockDim.x) dst[i] = src[i];
+}
+
 }  // namespace fa

@@ -648,6 +648,59 @@ fa_status launch_qkv(const fa_kv_layer *L, const fa_qkv_weights *w, const void *
   return launch_gemm<T>(T_, N, w->hidden, epi, x, w->weight, L->dtype, stream, "qkv_rope_cache");
 }
 
+// Layers of one bundle: every layer must share layer 0's shape and dtype (one model's pool).
+fa_status bundle_params(const fa_kv_layer *layers, int32_t num_layers,
+                               const int32_t *block_ids, int32_t num_logical, const void *payload,
+                               fa::BundleParams *p, int *vec, const char *who) {
+  if (!layers) return fail(FA_EINVAL, "%s: layers is NULL", who);
+  if (num_layers <= 0 || num_layers > FA_MAX_COPY_LAYERS)
+    return fail(FA_EINVAL, "%s: num_layers %d outside [1, %d]", who, num_layers, FA_MAX_COPY_LAYERS);
+  if (num_logical < 0 || num_logical > 65535)
+    return fail(FA_EINVAL, "%s: num_blocks %d outside [0, 65535]", who, num_logical);
+  const fa_kv_layer &L0 = layers[0];
+  for (int l = 0; l < num_layers; ++l) {
+    if (fa_status s = check_layer(&layers[l], who); s != FA_OK) return s;
+    const fa_kv_layer &L = layers[l];
+    if (L.num_blocks != L0.num_blocks || L.num_kv_heads != L0.num_kv_heads ||
+        L.block_size != L0.block_size || L.head_dim != L0.head_dim || L.dtype != L0.dtype)
+      return fail(FA_EINVAL, "%s: layer %d shape/dtype differs from layer 0", who, l);
+    p->k[l] = static_cast<char *>(L.k_cache);
+    p->v[l] = static_cast<char *>(L.v_cache);
+  }
+  if (num_logical > 0 && (!block_ids || !payload))
+    return fail(FA_EINVAL, "%s: NULL block_ids/payload", who);
+  p->block_ids = block_ids;
+  p->payload = static_cast<char *>(const_cast<void *>(payload));
+  p->block_bytes = int64_t(L0.num_kv_heads) * L0.block_size * L0.head_dim * dtype_size(L0.dtype);
+  p->num_logical = num_logical;
+  p->num_layers = num_layers;
+  p->num_blocks = L0.num_blocks;
+  int v = 16;
+  auto fits = [&](int w) {
+    if (p->block_bytes % w || !aligned(payload, w)) return false;
+    for (int l = 0; l < num_layers; ++l)
+      if (!aligned(p->k[l], w) || !aligned(p->v[l], w)) return false;
+    return true;
+  };
+  while (v > 2 && !fits(v)) v >>= 1;
+  if (!fits(v)) return fail(FA_EINVAL, "%s: misaligned caches or payload", who);
+  *vec = v;
+  return FA_OK;
+}
+
+template <bool kImport>
+fa_status bundle_launch(const fa::BundleParams &p, int vec, cudaStream_t stream,
+                               const char *who) {
+  dim3 grid(2 * p.num_layers, p.num_logical);
+  switch (vec) {
+    case 16: fa::bundle_payload_kernel<16, kImport><<<grid, 256, 0, stream>>>(p); break;
+    case 8: fa::bundle_payload_kernel<8, kImport><<<grid, 256, 0, stream>>>(p); break;
+    case 4: fa::bundle_payload_kernel<4, kImport><<<grid, 256, 0, stream>>>(p); break;
+    default: fa::bundle_payload_kernel<2, kImport><<<grid, 256, 0, stream>>>(p); break;
+  }
+  return check_launch(who);
+}
+
 }  // namespace
 
 extern "C" {
@@ -810,6 +863,39 @@ fa_status fa_read_block(const fa_kv_layer *layer, int32_t block_id, void *key, v
       size_t(block_id) * layer->num_kv_heads * layer->block_size * layer->head_dim * dtype_size(layer->dtype);
   return block_copy(layer, block_id, key, static_cast<const char *>(layer->k_cache) + off, value,
                     static_cast<const char *>(layer->v_cache) + off, stream, "read_block");
+}
+
+size_t fa_bundle_payload_bytes(const fa_kv_layer *layer, int32_t num_layers,
+                               int32_t num_blocks) {
+  if (!layer || num_layers <= 0 || num_blocks <= 0) return 0;
+  return size_t(num_blocks) * size_t(num_layers) * 2 * size_t(layer->num_kv_heads) *
+         size_t(layer->block_size) * size_t(layer->head_dim) * dtype_size(layer->dtype);
+}
+
+fa_status fa_export_bundle_payload(const fa_kv_layer *layers, int32_t num_layers,
+                                   const int32_t *block_ids, int32_t num_blocks, void *payload,
+                                   fa_stream_t stream) {
+  const char *who = "export_bundle_payload";
+  fa::BundleParams p{};
+  int vec = 16;
+  if (fa_status s = bundle_params(layers, num_layers, block_ids, num_blocks, payload, &p, &vec, who);
+      s != FA_OK)
+    return s;
+  if (num_blocks == 0) return ok();
+  return bundle_launch<false>(p, vec, stream, who);
+}
+
+fa_status fa_import_bundle_payload(const fa_kv_layer *layers, int32_t num_layers,
+                                   const int32_t *block_ids, int32_t num_blocks,
+                                   const void *payload, fa_stream_t stream) {
+  const char *who = "import_bundle_payload";
+  fa::BundleParams p{};
+  int vec = 16;
+  if (fa_status s = bundle_params(layers, num_layers, block_ids, num_blocks, payload, &p, &vec, who);
+      s != FA_OK)
+    return s;
+  if (num_blocks == 0) return ok();
+  return bundle_launch<true>(p, vec, stream, who);
 }
 
 size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,

@@ -88,6 +88,39 @@ def read_block(k_cache, v_cache, block_id: int, key_out, value_out, stream=None)
                               _stream(stream)), "read_block")
 
 
+def bundle_payload_bytes(k_caches, v_caches, num_blocks: int) -> int:
+    layer = layer_desc(k_caches[0], v_caches[0])
+    return int(lib().fa_bundle_payload_bytes(ctypes.byref(layer), len(k_caches), num_blocks))
+
+
+def export_bundle_payload(k_caches, v_caches, block_ids, payload=None, stream=None):
+    """FLKV payload of the physical blocks `block_ids` (logical order) of every layer, in one
+    launch: for block, for layer, K then V (kv_heads, bs, d). Returns the device uint8 payload
+    (`payload` if given); the caller copies it to the host in one transfer."""
+    layers = (FaKvLayer * len(k_caches))(*[layer_desc(k, v) for k, v in zip(k_caches, v_caches)])
+    ids = _i32(block_ids, "block_ids")
+    n = bundle_payload_bytes(k_caches, v_caches, ids.numel())
+    if payload is None:
+        payload = torch.empty(n, dtype=torch.uint8, device=k_caches[0].device)
+    elif payload.numel() * payload.element_size() < n or not payload.is_contiguous():
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"payload must be contiguous with >= {n} bytes")
+    check(lib().fa_export_bundle_payload(layers, len(k_caches), _ptr(ids), ids.numel(),
+                                         _ptr(payload), _stream(stream)), "export_bundle_payload")
+    return payload
+
+
+def import_bundle_payload(k_caches, v_caches, block_ids, payload, stream=None) -> None:
+    """The mirror of export_bundle_payload: payload (device) -> physical blocks `block_ids` of
+    every layer, in one launch."""
+    layers = (FaKvLayer * len(k_caches))(*[layer_desc(k, v) for k, v in zip(k_caches, v_caches)])
+    ids = _i32(block_ids, "block_ids")
+    n = bundle_payload_bytes(k_caches, v_caches, ids.numel())
+    if payload.numel() * payload.element_size() < n or not payload.is_contiguous():
+        raise _lib.FlourAttnError(_lib.FA_EINVAL, f"payload must be contiguous with >= {n} bytes")
+    check(lib().fa_import_bundle_payload(layers, len(k_caches), _ptr(ids), ids.numel(),
+                                         _ptr(payload), _stream(stream)), "import_bundle_payload")
+
+
 # ---- attention ----------------------------------------------------------------------------
 
 def workspace_size(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,

@@ -147,6 +147,33 @@ FA_API fa_status fa_write_block(const fa_kv_layer *layer, int32_t block_id, cons
 FA_API fa_status fa_read_block(const fa_kv_layer *layer, int32_t block_id, void *key, void *value,
                         fa_stream_t stream);
 
+/* ---- FLKV bundle payload: KvCache::export/import_prefix_bundle (src/models/common/cache.rs:
+ * 166-349), payload order of src/kv_cache/bundle.rs:15-22 ---------------------------------- */
+
+/* Bytes of the payload of `num_blocks` logical blocks over `num_layers` layers shaped like
+ * `layer`: num_blocks * num_layers * 2 * (num_kv_heads * block_size * head_dim * dtype size). */
+FA_API size_t fa_bundle_payload_bytes(const fa_kv_layer *layer, int32_t num_layers,
+                                      int32_t num_blocks);
+
+/* Export: gather, in one launch, the K and V of every layer of the physical blocks
+ * block_ids[0..num_blocks) (device int32, the sequence's logical order) into `payload` (device,
+ * fa_bundle_payload_bytes bytes) in the FLKV payload order:
+ *     for block in 0..num_blocks: for layer in 0..num_layers: K then V, (kv_heads, bs, head_dim)
+ * The caller then moves the payload to the host with one copy (the reference's export writes the
+ * same bytes, block by block, from its CPU pool). All layers must share one shape and dtype; at
+ * most FA_MAX_COPY_LAYERS layers. A block id outside [0, num_blocks of the pool) zero-fills its
+ * pieces and sets FA_DEVERR_BLOCK_ID. Payload and pools must not overlap. */
+FA_API fa_status fa_export_bundle_payload(const fa_kv_layer *layers, int32_t num_layers,
+                                          const int32_t *block_ids, int32_t num_blocks,
+                                          void *payload, fa_stream_t stream);
+
+/* Import: the mirror scatter, payload (device, same order) -> physical blocks block_ids[b] of
+ * every layer, as KvCache::import_prefix_bundle's write_block loop does (cache.rs:304-321). Ids
+ * must be distinct; a bad id is skipped and sets FA_DEVERR_BLOCK_ID. */
+FA_API fa_status fa_import_bundle_payload(const fa_kv_layer *layers, int32_t num_layers,
+                                          const int32_t *block_ids, int32_t num_blocks,
+                                          const void *payload, fa_stream_t stream);
+
 /* ---- paged attention: backend::cpu::paged_attention (src/backend/cpu.rs:57-112) ------- */
 
 /* Bytes of workspace the attention entry points need for these sizes (split-K partials and

@@ -167,3 +167,66 @@ def test_bundle_export_payload_order_through_read_block(device):
     want = oracle.bundle_export([to_numpy(x) for x in cache.pool.k_pools],
                                 [to_numpy(x) for x in cache.pool.v_pools], blocks)
     np.testing.assert_array_equal(payload, want)
+
+
+def _bundle_pools(device, layers, nb, kvh, d, dtype, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    ks = [torch.randn((nb, kvh, 16, d), device=device, generator=g).to(dtype) for _ in range(layers)]
+    vs = [torch.randn((nb, kvh, 16, d), device=device, generator=g).to(dtype) for _ in range(layers)]
+    return ks, vs
+
+
+def test_bundle_payload_export_one_launch_matches_oracle(device):
+    # A 2048-token prefix of Llama-3-8B: 128 blocks x 32 layers, gathered in one launch into the
+    # FLKV payload order (bundle.rs:15-22), bit-exact against the oracle's restatement.
+    L, nb = 32, 512
+    ks, vs = _bundle_pools(device, L, nb, 8, 128, torch.bfloat16, 40)
+    ids = torch.from_numpy(np.random.default_rng(40).permutation(nb)[:128].astype(np.int32)).to(device)
+    payload = ops.export_bundle_payload(ks, vs, ids)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert payload.numel() == 128 * L * 2 * 8 * 16 * 128 * 2
+    want = oracle.bundle_export([to_numpy(x) for x in ks], [to_numpy(x) for x in vs],
+                                ids.cpu().numpy())
+    np.testing.assert_array_equal(payload.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("dtype,kvh,d", [(torch.float32, 2, 64), (torch.float16, 4, 128),
+                                         (torch.bfloat16, 1, 96)])
+def test_bundle_payload_round_trip_and_neighbours(device, dtype, kvh, d):
+    # Export from one pool, import into other physical blocks of a second pool (the importing
+    # node's own allocation): bit-exact against the oracle import, every other block untouched.
+    L, nb, n = 3, 40, 7
+    ks, vs = _bundle_pools(device, L, nb, kvh, d, dtype, 41)
+    src = torch.tensor([5, 0, 39, 12, 7, 8, 21], dtype=torch.int32, device=device)
+    payload = ops.export_bundle_payload(ks, vs, src)
+    k2, v2 = _bundle_pools(device, L, nb, kvh, d, dtype, 42)
+    k2_np, v2_np = [to_numpy(x) for x in k2], [to_numpy(x) for x in v2]
+    dst = torch.tensor([30, 31, 1, 2, 17, 18, 3], dtype=torch.int32, device=device)
+    ops.import_bundle_payload(k2, v2, dst, payload)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    oracle.bundle_import(k2_np, v2_np, dst.cpu().numpy(), payload.cpu().numpy())
+    for l in range(L):
+        np.testing.assert_array_equal(to_numpy(k2[l]), k2_np[l])
+        np.testing.assert_array_equal(to_numpy(v2[l]), v2_np[l])
+        assert torch.equal(k2[l][dst.long()], ks[l][src.long()])
+
+
+def test_bundle_payload_bad_block_id(device):
+    L, nb = 2, 8
+    ks, vs = _bundle_pools(device, L, nb, 2, 64, torch.bfloat16, 43)
+    ops.device_status()
+    ids = torch.tensor([1, nb, 2], dtype=torch.int32, device=device)
+    payload = ops.export_bundle_payload(ks, vs, ids)
+    torch.cuda.synchronize()
+    assert ops.device_status() & _lib.FA_DEVERR_BLOCK_ID
+    piece = 2 * 16 * 64 * 2
+    p = payload.view(3, L, 2, piece)
+    assert int(p[1].abs().sum()) == 0  # the bad block's pieces are zero-filled
+    assert torch.equal(p[0, 0, 0].view(torch.bfloat16).view(2, 16, 64), ks[0][1])
+    before = [k.clone() for k in ks]
+    ops.import_bundle_payload(ks, vs, ids, payload)
+    torch.cuda.synchronize()
+    assert ops.device_status() & _lib.FA_DEVERR_BLOCK_ID
+    assert all(torch.equal(a, b) for a, b in zip(ks, before))  # same data back in blocks 1, 2
