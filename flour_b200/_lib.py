@@ -113,6 +113,8 @@ SIGNATURES = {
     "fa_bundle_payload_bytes": (_SZ, [_LP, _I32, _I32]),
     "fa_export_bundle_payload": (_I32, [_LP, _I32, _P, _I32, _P, _P]),
     "fa_import_bundle_payload": (_I32, [_LP, _I32, _P, _I32, _P, _P]),
+    "fa_gemm_tile_width": (_I32, [_I32, _I32, _I32]),
+    "fa_workspace_reset": (_I32, [_P]),
     "fa_qkv_rope_cache": (_I32, [_LP, _WP, _P, _P, _P, _I32, _P, _P]),
     "fa_o_proj_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P]),
     "fa_last_token_logits": (_I32, [_P, _P, _I32, _I32, _P, _F, _P, _I32, _I32, _I32, _P, _P, _P]),

@@ -141,6 +141,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int n_rep = p.n_rep;
+  // A following kernel launched with programmatic serialization (the projection GEMMs) may
+  // start its prologue and weight loads once every CTA of this grid has started.
+  if (tid == 0) pdl_trigger();
 
   const int ctx = p.context_lens[b];
   if (ctx < 1 || ctx > p.max_context_len || int64_t(ctx) > int64_t(p.max_blocks_per_seq) * kPage) {

@@ -115,6 +115,16 @@ template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
   return __half22float2(h);
 }
 
+// ---- programmatic dependent launch ------------------------------------------------------
+// pdl_trigger: this CTA no longer holds back the next kernel on the stream, which may start
+// (where it was launched with programmatic stream serialization) as SMs free up. pdl_wait: block
+// until the preceding kernel has completed and its writes are visible. Both are no-ops for a
+// launch without the programmatic attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- mbarrier -------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -162,6 +172,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled prefetch of one box into L2 (no shared memory, no completion signal).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 // 2-D tiled load of one box into shared memory, completing on `bar` (complete_tx bytes).

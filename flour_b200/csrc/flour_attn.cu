@@ -513,7 +513,20 @@ fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, cons
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "%s: set smem attribute: %s", who, cudaGetErrorString(e));
   const int grid = int(std::min<int64_t>(sm_count(), int64_t(s.tiles_m) * s.tiles_n));
-  kern<<<grid, fa::kGemmThreads, C::kAlloc, stream>>>(s, epi, ta, tb);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(fa::kGemmThreads);
+  cfg.dynamicSmemBytes = C::kAlloc;
+  cfg.stream = stream;
+  // Programmatic dependent launch: the prologue and the first weight stages overlap the tail of
+  // the preceding kernel; the kernel waits for it before touching activations or outputs.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, s, epi, ta, tb);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return check_launch(who);
 }
 
@@ -535,13 +548,16 @@ fa_status launch_gemm_splitk_rows(int M, int N, int K, int ranks, const Epi &epi
   cfg.blockDim = dim3(fa::kGemmThreads);
   cfg.dynamicSmemBytes = C::kAlloc;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = unsigned(ranks);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch (as for the unsplit GEMM).
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, s, epi, ta, tb);
   if (e != cudaSuccess) return fail(FA_ECUDA, "%s: cluster launch: %s", who, cudaGetErrorString(e));
   return check_launch(who);
@@ -898,6 +914,13 @@ fa_status fa_import_bundle_payload(const fa_kv_layer *layers, int32_t num_layers
   return bundle_launch<true>(p, vec, stream, who);
 }
 
+fa_status fa_workspace_reset(const void *workspace) {
+  if (!workspace) return fail(FA_EINVAL, "workspace_reset: workspace is NULL");
+  std::lock_guard<std::mutex> lock(g_ticket_mu);
+  g_ticket_state.erase(reinterpret_cast<uintptr_t>(workspace));
+  return ok();
+}
+
 size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
                                          int32_t head_dim, int32_t max_context_len,
                                          int32_t max_seqlen_q) {
@@ -1046,6 +1069,12 @@ fa_status fa_paged_decode_noalloc(const fa_kv_layer *layer, const void *query, v
   return launch_decode(layer, query, out, context_lens, block_tables, max_blocks_per_seq, num_seqs,
                        num_heads, n_rep, max_context_len, scale, FA_SCORES_F32, scratch,
                        FA_NOALLOC_DECODE_SCRATCH_BYTES, stream, nullptr, false);
+}
+
+int32_t fa_gemm_tile_width(int32_t M, int32_t N, int32_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (gemm_split_ranks<__nv_bfloat16, fa::F32Epilogue>(M, N, K) >= 2) return 128;
+  return gemm_bn(M, N);
 }
 
 fa_status fa_qkv_rope_cache(const fa_kv_layer *layer, const fa_qkv_weights *w, const void *x,

@@ -290,6 +290,7 @@ __global__ void __launch_bounds__(kNormThreads)
                           const T *weight, float eps, int H, T *out) {
   __shared__ float s_red[kNormThreads / 32];
   const int seq = blockIdx.x, tid = threadIdx.x;
+  if (tid == 0) pdl_trigger();  // the lm_head GEMM may start loading weights
   const int a = cu_seqlens[seq], b = cu_seqlens[seq + 1];
   T *o = out + size_t(seq) * H;
   if (!(a >= 0 && b > a && b <= total_tokens)) {
@@ -350,12 +351,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *s_tmem;
+  if (tid == 0) pdl_trigger();  // the next kernel may start its prologue as SMs free up
 
   if (warp == 0) {
     // ================= TMA producer =================
     if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
+      // Weights do not depend on the preceding kernel: the first tile's first ring stages of B
+      // are requested before waiting for it (programmatic dependent launch), A after.
+      const int pre = blockIdx.x < tiles ? min(num_k, C::kStages) : 0;
+      {
+        const int n0 = blockIdx.x % s.tiles_n;
+        for (int st = 0; st < pre; ++st) {
+          mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
+          tma_load_2d(sbase + st * C::kStageBytes + C::kABytes, &tm_b, bar(C::FULL + st),
+                      st * kGemmBK, n0 * BN);
+        }
+      }
+      pdl_wait();
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -364,10 +378,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int st = it % C::kStages;
           if (it >= C::kStages && !(ok = mbar_wait(bar(C::EMPTY + st), ((it / C::kStages) - 1) & 1)))
             break;
-          mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
           const uint32_t a = sbase + st * C::kStageBytes;
+          if (it >= pre) mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
           tma_load_2d(a, &tm_a, bar(C::FULL + st), kb * kGemmBK, m * 128);
-          tma_load_2d(a + C::kABytes, &tm_b, bar(C::FULL + st), kb * kGemmBK, n * BN);
+          if (it >= pre) tma_load_2d(a + C::kABytes, &tm_b, bar(C::FULL + st), kb * kGemmBK, n * BN);
         }
       }
       if (!ok) report(FA_DEVERR_TIMEOUT);
@@ -406,6 +420,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ================= epilogue: thread = output row of the tile =================
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const uint32_t lane_off = uint32_t(q * 32) << 16;
+    pdl_wait();  // the epilogue reads and writes memory the preceding kernel may use
     int tc_n = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc_n) {
       const int buf = tc_n & 1;
@@ -554,20 +569,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc::fence_after();
   cluster_sync();  // every CTA's barriers are initialised before any remote arrive
   const uint32_t tmem = *s_tmem;
+  if (tid == 0) pdl_trigger();  // the next kernel may start its prologue as SMs free up
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
+      // Weights do not depend on the preceding kernel: the first ring stages of B are requested
+      // before waiting for it (programmatic dependent launch), A after.
+      const int pre = min(kb1 - kb0, C::kStages);
+      for (int st = 0; st < pre; ++st) {
+        mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
+        tma_load_2d(sbase + st * C::kStageBytes + C::kABytes, &tm_b, bar(C::FULL + st),
+                    (kb0 + st) * kGemmBK, n * BN);
+      }
+      // The rest of this CTA's weight slice goes to L2 meanwhile (the decode-batch GEMMs this
+      // kernel serves stream weights that are read exactly once).
+      for (int kb = kb0 + pre; kb < kb1; ++kb) tma_prefetch_l2_2d(&tm_b, kb * kGemmBK, n * BN);
+      pdl_wait();
       bool ok = true;
       for (int kb = kb0, it = 0; kb < kb1 && ok; ++kb, ++it) {
         const int st = it % C::kStages;
         if (it >= C::kStages && !(ok = mbar_wait(bar(C::EMPTY + st), ((it / C::kStages) - 1) & 1)))
           break;
-        mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
         const uint32_t a = sbase + st * C::kStageBytes;
+        if (it >= pre) mbar_arrive_expect_tx(bar(C::FULL + st), C::kStageBytes);
         tma_load_2d(a, &tm_a, bar(C::FULL + st), kb * kGemmBK, m * 128);
-        tma_load_2d(a + C::kABytes, &tm_b, bar(C::FULL + st), kb * kGemmBK, n * BN);
+        if (it >= pre) tma_load_2d(a + C::kABytes, &tm_b, bar(C::FULL + st), kb * kGemmBK, n * BN);
       }
       if (!ok) report(FA_DEVERR_TIMEOUT);
     }
@@ -597,6 +625,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t lane_off = uint32_t(q * 32) << 16;
     const int r = q * 32 + lane;  // tile row of this thread's TMEM lane
     float *part = reinterpret_cast<float *>(smem);
+    pdl_wait();  // the epilogue reads and writes memory the preceding kernel may use
     bool ok = __all_sync(0xffffffffu, mbar_wait(bar(C::AFULL), 0));
     if (ok) {
       tc::fence_after();

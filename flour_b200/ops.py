@@ -142,6 +142,9 @@ class Workspace:
             return self.buf
         if self.buf is None or self.buf.numel() < nbytes:
             self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            # A fresh zero-filled buffer: bookkeeping kept for an earlier buffer at the same
+            # address (the caching allocator reuses addresses) no longer applies.
+            check(lib().fa_workspace_reset(_ptr(self.buf)), "workspace_reset")
         return self.buf
 
 

@@ -186,6 +186,15 @@ FA_API size_t fa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_he
                                          int32_t num_kv_heads, int32_t head_dim,
                                          int32_t max_context_len, int32_t max_seqlen_q);
 
+/* The library remembers, per workspace base pointer, which merge tickets are known to be zero
+ * (and which smaller calls were recorded into CUDA graphs, whose replays leave partials behind),
+ * so that a workspace reused across shapes is zeroed only where needed. Call this when a
+ * workspace at `workspace` is freshly zero-filled, for example a new allocation that may reuse
+ * the address of an earlier workspace, once no CUDA graph that recorded calls with the earlier
+ * buffer will be replayed: the earlier buffer's bookkeeping no longer applies. No counterpart in
+ * the reference. */
+FA_API fa_status fa_workspace_reset(const void *workspace);
+
 /* General entry, same contract as paged_attention(q, blocks, n_rep, scale) for a batch of
  * sequences with varying query counts (decode when every sequence has one query token).
  *   query/out       device [total_q, num_heads, head_dim], pool dtype
@@ -337,6 +346,17 @@ FA_API fa_status fa_last_token_logits(const void *hidden, const int32_t *cu_seql
                                       const void *norm_weight, float rms_eps, const void *lm_head,
                                       int32_t hidden_size, int32_t vocab, int32_t dtype,
                                       void *normed_out, float *logits_out, fa_stream_t stream);
+
+/* Width in output columns of the tiles the projection GEMMs above use for an M x N x K problem
+ * (128 or 256; 128 when K is split over a thread-block cluster), as chosen on the current device.
+ * A reporting aid: the choice depends only on the shape and the device's SM count. No
+ * counterpart in the reference. */
+FA_API int32_t fa_gemm_tile_width(int32_t M, int32_t N, int32_t K);
+
+/* The projection GEMMs (fa_qkv_rope_cache, fa_o_proj_residual, fa_last_token_logits) are
+ * launched with programmatic stream serialization: each may start its prologue and request its
+ * first weight tiles while the preceding kernel on the stream finishes, and waits for that
+ * kernel's completion before it reads activations or writes outputs. */
 
 /* ---- head-sharded decode (tensor parallel over KV heads, one process per GPU) ----------
  * The reference runs attention on one CPU and has no sharding (its plan shards sequences,
