@@ -141,9 +141,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int n_rep = p.n_rep;
-  // A following kernel launched with programmatic serialization (the projection GEMMs) may
-  // start its prologue and weight loads once every CTA of this grid has started.
+  // Programmatic dependent launch: a following kernel launched with programmatic serialization
+  // (the next decode, the projection GEMMs) may start once every CTA of this grid has started;
+  // this grid's own inputs, workspace and outputs are touched only after the preceding kernel
+  // has completed (a no-op wait when this launch has no programmatic dependency).
   if (tid == 0) pdl_trigger();
+  pdl_wait();
 
   const int ctx = p.context_lens[b];
   if (ctx < 1 || ctx > p.max_context_len || int64_t(ctx) > int64_t(p.max_blocks_per_seq) * kPage) {
@@ -428,6 +431,10 @@ __global__ void tp_sync_kernel(TpFlagSlots publish_to, const uint32_t *my_flags,
                                unsigned long long timeout_ns) {
   __shared__ uint32_t s_epoch;
   const int s = threadIdx.x;
+  // Launched with programmatic serialization: started early, it publishes only once the
+  // preceding decode (its peer stores included) has completed.
+  if (s == 0) pdl_trigger();
+  pdl_wait();
   if (s == 0) {
     uint32_t e = epoch;
     if (e == 0) {

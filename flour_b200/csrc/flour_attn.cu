@@ -172,8 +172,20 @@ fa_status launch_decode_t(const fa::DecodeParams &p, const CUtensorMap &tk, cons
   auto kern = fa::paged_decode_kernel<T, HD, NSTAGE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "decode: set smem attribute: %s", cudaGetErrorString(e));
-  dim3 grid(p.max_splits, p.num_kv_heads, p.num_seqs);
-  kern<<<grid, fa::kDecodeThreads, S::kAlloc, stream>>>(p, tk, tv);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.max_splits, p.num_kv_heads, p.num_seqs);
+  cfg.blockDim = dim3(fa::kDecodeThreads);
+  cfg.dynamicSmemBytes = S::kAlloc;
+  cfg.stream = stream;
+  // Programmatic dependent launch: the CTAs may start while the preceding kernel finishes and
+  // wait for it (griddepcontrol.wait) before touching any input, workspace or output.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "paged_decode: launch: %s", cudaGetErrorString(e));
   return check_launch("paged_decode");
 }
 
@@ -1280,9 +1292,20 @@ fa_status fa_tp_sync(const fa_tp_group *group, uint32_t epoch, int32_t mode, int
     return fail(FA_ERANGE, "%s: timeout_ns %lld outside [1e3, 1e10]", who, (long long)timeout_ns);
   fa::TpFlagSlots slots{};
   for (int r = 0; r < group->tp; ++r) slots.slot[r] = group->flags[r] + group->rank;
-  fa::tp_sync_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      slots, group->flags[group->rank], group->tp, epoch, group->epoch_counter, mode,
-      (unsigned long long)timeout_ns);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];  // programmatic dependent launch, as for the decode
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, fa::tp_sync_kernel, slots,
+                         static_cast<const uint32_t *>(group->flags[group->rank]), int(group->tp),
+                         epoch, group->epoch_counter, int(mode), (unsigned long long)timeout_ns);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return check_launch(who);
 }
 
