@@ -5,6 +5,7 @@
     python tests/profile_case.py prefill [--launches 3]
     python tests/profile_case.py qkv     [--launches 3] [--tokens 13490]
     python tests/profile_case.py oproj   [--launches 3] [--tokens 13490]
+    python tests/profile_case.py bundle  [--launches 3]
 
 Not collected by pytest (no test_ prefix); the profiles/*.md summaries name the command line
 that made them.
@@ -34,7 +35,7 @@ from flour_b200.workloads import LLAMA8B, c2_contexts, c4_contexts, make_c3, mak
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "longctx", "prefill", "qkv", "oproj"])
+    ap.add_argument("case", choices=["decode", "longctx", "prefill", "qkv", "oproj", "bundle"])
     ap.add_argument("--tokens", type=int, default=13490)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--batch", type=int, default=64)
@@ -78,6 +79,22 @@ def main() -> int:
             flops = 2 * T * hq * d * hidden
         torch.cuda.synchronize()
         print(f"{a.case}: {flops} algorithmic FLOPs/launch")
+    elif a.case == "bundle":
+        # FLKV export of 128 blocks x 32 layers (Llama-3-8B heads, 268 MB payload) from 32 pools
+        # of 512 blocks (1 GB): the one-launch gather.
+        import numpy as np
+        g = torch.Generator(device=dev).manual_seed(a.seed)
+        ks = [torch.randn((512, 8, 16, 128), device=dev, generator=g).to(torch.bfloat16)
+              for _ in range(32)]
+        vs = [torch.randn((512, 8, 16, 128), device=dev, generator=g).to(torch.bfloat16)
+              for _ in range(32)]
+        ids = torch.from_numpy(np.random.default_rng(a.seed).permutation(512)[:128].astype(np.int32)
+                               ).to(dev)
+        payload = torch.empty(ops.bundle_payload_bytes(ks, vs, 128), dtype=torch.uint8, device=dev)
+        for _ in range(1 + a.launches):
+            ops.export_bundle_payload(ks, vs, ids, payload)
+        torch.cuda.synchronize()
+        print(f"bundle: {2 * payload.numel()} algorithmic bytes/launch (read + write)")
     else:
         b = make_c3(dev, seed=a.seed)
         ops.reshape_and_cache(b.k_caches[0], b.v_caches[0], b.key, b.value, b.slot_mapping)
