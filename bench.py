@@ -12,8 +12,9 @@ fa_paged_decode, two launches per layer). Each layer's pool
 (~0.6 GB) is larger than L2, so no L2 flush is needed between timed iterations.
 
 Metric value: algorithmic KV bytes read per step (sum ctx x Hkv x d x 2 [K,V] x 2 B, plus the
-q/out/table bytes) x steps x N GPUs / max-over-ranks device time. Multi-GPU: sequence sharding,
-every rank owns its own pool and batch (seed + rank); no collective on the data path ("weak").
+q/out/table bytes) summed over the N GPUs x steps / max-over-ranks device time. Multi-GPU:
+sequence sharding, every rank owns its own pool and batch of the same context lengths (values
+seeded per rank), so the work per GPU is fixed; no collective on the data path ("weak").
 
 Extra objects on the same JSON line: ``roofline`` (decode kernel: algorithmic bytes per launch
 over its average launch duration in the timed region, which holds only those launches;
@@ -333,7 +334,9 @@ def run_ours(args):
     seed = args.seed + rank
     h = LLAMA8B
     scale = 1.0 / math.sqrt(h.head_dim)
-    batch = make_decode(h, c2_contexts(seed), torch.bfloat16, dev, seed, num_layers=NUM_LAYERS)
+    # Weak scaling: every rank decodes a batch with the same context lengths (the same KV bytes
+    # per step), filled with its own seeded values.
+    batch = make_decode(h, c2_contexts(args.seed), torch.bfloat16, dev, seed, num_layers=NUM_LAYERS)
     gen = torch.Generator(device=dev).manual_seed(seed + 1)
     B = batch.num_seqs
     qs = [torch.randn((B, h.num_heads, h.head_dim), device=dev, generator=gen).to(torch.bfloat16)
@@ -424,7 +427,10 @@ def run_ours(args):
     own_ms = e0.elapsed_time(e1)
     ms = max_over_ranks(own_ms)
     ms_per_step = ms / args.steps
-    value = kv_bytes_step * args.steps * world / (ms / 1e3) / 1e9
+    # Whole-job bytes: the sum of every rank's bytes (equal by construction) over the slowest
+    # rank's time.
+    job_bytes_step = sum(b for (b,) in gather([kv_bytes_step]))
+    value = job_bytes_step * args.steps / (ms / 1e3) / 1e9
     assert ops.device_status() == 0
     # Per-rank step time, decode fraction of the measured peak, SM clock and power (each rank's
     # own sampler over its own GPU), so a slow GPU in a multi-GPU run is named in the record.

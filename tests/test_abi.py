@@ -101,3 +101,11 @@ def test_decode_workspace_too_small_is_rejected_without_launch():
                            0, ctypes.c_void_p(0x100000), need - 1, None)
     assert st == _lib.FA_ERANGE
     assert b"workspace" in L.fa_last_error_message()
+
+
+def test_workspace_reset_rejects_null_and_accepts_any_pointer():
+    L = lib()
+    assert L.fa_workspace_reset(None) == _lib.FA_EINVAL
+    assert b"NULL" in L.fa_last_error_message()
+    # Forgetting a pointer the library never saw is a no-op success (host bookkeeping only).
+    assert L.fa_workspace_reset(ctypes.c_void_p(0x123400)) == _lib.FA_OK

@@ -276,3 +276,14 @@ def test_last_token_logits_rejects_bad_arguments(device):
         ops.last_token_logits(hidden, cu, lm[:500], w)        # vocab not a multiple of 32
     with pytest.raises(_lib.FlourAttnError):
         ops.last_token_logits(hidden.float(), cu, lm, w)      # f32 hidden
+
+
+def test_gemm_tile_width_query(device):
+    L = _lib.lib()
+    # The C2 lm_head (64 rows, 128256 columns): 128-column tiles (7 waves of 128 columns on the
+    # busiest SM instead of 4 of 256). A C3-sized QKV projection fills the GPU with 256-wide
+    # tiles; a decode-batch QKV splits K over a cluster (128-wide tiles).
+    assert L.fa_gemm_tile_width(64, 128256, 4096) == 128
+    assert L.fa_gemm_tile_width(15401, 6144, 4096) == 256
+    assert L.fa_gemm_tile_width(64, 6144, 4096) == 128
+    assert L.fa_gemm_tile_width(0, 6144, 4096) == 0
