@@ -415,9 +415,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 }
 
 // Head-sharded groups: mark this rank's preceding launches on the stream complete and/or wait
-// for the other ranks. Publish (thread 0): epoch e (the host's, or with epoch 0 the next device
-// epoch *counter + 1) goes into slot [rank] of every rank's flag array with a system-scope
-// release. Stream order already completed the preceding decode, its peer stores included.
+// for the other ranks. Publish: epoch e (the host's, or with epoch 0 the next device epoch
+// *counter + 1, taken by thread 0) goes into slot [rank] of every rank's flag array, thread r
+// storing to rank r with a system-scope release, so the tp stores go out in parallel rather
+// than one release after another. Every thread has waited for the preceding decode (its peer
+// stores included) to complete, so each release covers them.
 // Wait (thread s < tp): poll this rank's flags[s] until it reaches e (wrap-around order; with
 // epoch 0, e = *counter), bounded by device time and an iteration cap; on expiry it reports
 // FA_DEVERR_TIMEOUT and returns.
@@ -441,17 +443,14 @@ __global__ void tp_sync_kernel(TpFlagSlots publish_to, const uint32_t *my_flags,
       e = *counter + ((mode & kTpPublish) ? 1u : 0u);
       if (mode & kTpPublish) *counter = e;
     }
-    if (mode & kTpPublish) {
-      __threadfence_system();
-      for (int r = 0; r < tp; ++r)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(publish_to.slot[r]), "r"(e)
-                     : "memory");
-    }
     s_epoch = e;
   }
   __syncthreads();
-  if (!(mode & kTpWait) || s >= tp) return;
   const uint32_t e = s_epoch;
+  if ((mode & kTpPublish) && s < tp)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(publish_to.slot[s]), "r"(e)
+                 : "memory");
+  if (!(mode & kTpWait) || s >= tp) return;
   unsigned long long t0, t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   const unsigned long long max_iters = timeout_ns / 64 + 4096;  // sleeps are >= ~100 ns
