@@ -37,6 +37,10 @@ struct ReshapeParams {
 template <int V>
 __global__ void __launch_bounds__(256) reshape_and_cache_kernel(const ReshapeParams p) {
   using VT = typename VecT<V>::type;
+  // Programmatic dependent launch: the next kernel (the attention that reads these slots) may
+  // be launched while this one runs; this one touches memory only after its predecessor is done.
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
   const int nvec = p.row_bytes / V;
   const int64_t total = int64_t(p.num_tokens) * p.num_kv_heads * nvec;
   for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;

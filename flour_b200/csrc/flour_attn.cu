@@ -383,7 +383,18 @@ fa_status launch_prefill_t(const fa::PrefillParams &p, const CUtensorMap &tq, co
   auto kern = fa::paged_prefill_kernel<T, kRef>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "prefill: set smem attribute: %s", cudaGetErrorString(e));
-  kern<<<grid_x, fa::kPfThreads, S::kAlloc, stream>>>(p, tq, tk, tv);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid_x));
+  cfg.blockDim = dim3(fa::kPfThreads);
+  cfg.dynamicSmemBytes = S::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];  // programmatic dependent launch: setup overlaps the predecessor
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p, tq, tk, tv);
+  if (e != cudaSuccess) return fail(FA_ECUDA, "paged_prefill: launch: %s", cudaGetErrorString(e));
   return check_launch("paged_prefill");
 }
 
@@ -809,12 +820,23 @@ fa_status fa_reshape_and_cache(const fa_kv_layer *layer, const void *key, const 
   const int64_t items = int64_t(num_tokens) * layer->num_kv_heads * (p.row_bytes / vec);
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((items + threads - 1) / threads, int64_t(kSmCount) * 16);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(blocks));
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];  // programmatic dependent launch, as for the attention kernels
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   switch (vec) {
-    case 16: fa::reshape_and_cache_kernel<16><<<unsigned(blocks), threads, 0, stream>>>(p); break;
-    case 8: fa::reshape_and_cache_kernel<8><<<unsigned(blocks), threads, 0, stream>>>(p); break;
-    case 4: fa::reshape_and_cache_kernel<4><<<unsigned(blocks), threads, 0, stream>>>(p); break;
-    default: fa::reshape_and_cache_kernel<2><<<unsigned(blocks), threads, 0, stream>>>(p); break;
+    case 16: e = cudaLaunchKernelEx(&cfg, fa::reshape_and_cache_kernel<16>, p); break;
+    case 8: e = cudaLaunchKernelEx(&cfg, fa::reshape_and_cache_kernel<8>, p); break;
+    case 4: e = cudaLaunchKernelEx(&cfg, fa::reshape_and_cache_kernel<4>, p); break;
+    default: e = cudaLaunchKernelEx(&cfg, fa::reshape_and_cache_kernel<2>, p); break;
   }
+  if (e != cudaSuccess) return fail(FA_ECUDA, "reshape_and_cache: launch: %s", cudaGetErrorString(e));
   return check_launch("reshape_and_cache");
 }
 

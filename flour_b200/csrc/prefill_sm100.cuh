@@ -139,12 +139,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int chunk = 2 * p.tq;
   T *out = static_cast<T *>(p.out);
 
-  // ---- chunk table: offs[s] = number of chunks of sequences < s -----------------------------
-  for (int s = tid; s < p.num_seqs; s += kPfThreads) {
-    const int len = p.cu_seqlens_q[s + 1] - p.cu_seqlens_q[s];
-    offs[s + 1] = len > 0 ? (len + chunk - 1) / chunk : 0;
-  }
+  // Programmatic dependent launch: barriers and TMEM are set up while the preceding kernel (the
+  // cache write of these tokens' K/V) finishes; global memory is touched only after it is done.
   if (tid == 0) {
+    pdl_trigger();
 #pragma unroll 1
     for (int i = 0; i < S::NBARS; ++i) {
       const int count = (i == S::PFULL || i == S::PFULL + 1) ? 256
@@ -158,6 +156,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == kPfMmaWarp) {
     tc::alloc(smem_u32(s_tmem), 512);
     tc::relinquish();
+  }
+  pdl_wait();
+  // ---- chunk table: offs[s] = number of chunks of sequences < s -----------------------------
+  for (int s = tid; s < p.num_seqs; s += kPfThreads) {
+    const int len = p.cu_seqlens_q[s + 1] - p.cu_seqlens_q[s];
+    offs[s + 1] = len > 0 ? (len + chunk - 1) / chunk : 0;
   }
   __syncthreads();
   if (warp == 0) {
