@@ -356,7 +356,9 @@ FA_API int32_t fa_gemm_tile_width(int32_t M, int32_t N, int32_t K);
 /* The projection GEMMs (fa_qkv_rope_cache, fa_o_proj_residual, fa_last_token_logits) are
  * launched with programmatic stream serialization: each may start its prologue and request its
  * first weight tiles while the preceding kernel on the stream finishes, and waits for that
- * kernel's completion before it reads activations or writes outputs. */
+ * kernel's completion before it reads activations or writes outputs. So are the decode kernels,
+ * fa_tp_sync, fa_reshape_and_cache and fa_paged_prefill, which set up only on-chip state before
+ * that wait. For a caller this changes nothing: stream order holds for every call. */
 
 /* ---- head-sharded decode (tensor parallel over KV heads, one process per GPU) ----------
  * The reference runs attention on one CPU and has no sharding (its plan shards sequences,
