@@ -804,7 +804,10 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier, 
     h, L = QWEN7B, 28
     ctx, is_pf, pf_len, cost = c5_plan(args.seed)
     mine = mixed_partition(cost, is_pf, world)[rank]
-    dec = [i for i in mine if not is_pf[i]]
+    # The batch builder hands the decode sequences over longest first (the order of a batch is
+    # its free choice): the long sequences' splits and merges then start first instead of
+    # trailing the launch (decode stream -9 % at N=1 and at the N=8 share, measured).
+    dec = sorted((i for i in mine if not is_pf[i]), key=lambda i: -int(ctx[i]))
     pf = [i for i in mine if is_pf[i]]
     ms = make_mixed_step(h, ctx[dec], pf_len[pf], torch.bfloat16, dev, args.seed + rank, L)
 
@@ -846,7 +849,8 @@ def run_c5(args, torch, ops, dev, stream, world, rank, max_over_ranks, barrier, 
     del ms
     res = {"config": "C5 mixed serving step: Qwen2-7B heads, 28 layers, 512 seqs (ctx ~ LogNormal"
                      "(ln 1024, 0.8) <= 8192), ~10 % new prefills L ~ U[256, 2048]; partitioned "
-                     "over ranks; seeded N(0,1) pools, queries and new K/V",
+                     "over ranks, each rank's decode sequences longest first; seeded N(0,1) "
+                     "pools, queries and new K/V",
            "scaling": "strong", "step_ms": round(ms_max, 4),
            "fastest_rank_step_ms": round(min(r[0] for r in per_rank), 4),
            "tokens_per_s": round(tokens / (ms_max / 1e3), 1),
