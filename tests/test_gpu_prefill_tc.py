@@ -177,3 +177,26 @@ def test_prefix_reuse_leaves_suffix_rows_unchanged(device, heads):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     assert max_abs(f32(out_warm), f32(out_cold)[rows]) <= 1e-2
+
+
+def test_more_sequences_than_one_launch_holds(device):
+    # A call with more than 2048 sequences runs as consecutive launches of the kernel on the
+    # stream (its sequence table lives in shared memory), which share the workspace's work
+    # counter and, with programmatic dependent launch, may be resident while the previous one
+    # finishes: every launch must still see the counter at zero and cover its own sequences.
+    rng = np.random.default_rng(71)
+    n = 2300
+    lens = rng.integers(1, 48, size=n)
+    prefix = np.minimum(lens - 1, rng.integers(0, 20, size=n)) // 16 * 16
+    b = build(device, Heads(8, 2, 128), lens, prefix, 72)
+    out = run_and_check(b)
+    # Once more on the same workspace: the counter came back to zero after the last launch.
+    h = b.heads
+    ws = ops.Workspace(device)
+    for _ in range(2):
+        again = ops.paged_prefill(b.q, b.k_caches[0], b.v_caches[0], b.cu_seqlens_q,
+                                  b.context_lens, b.block_tables, h.n_rep,
+                                  1 / math.sqrt(h.head_dim), b.max_seqlen_q, b.max_context_len, ws)
+        torch.cuda.synchronize()
+        assert torch.equal(again, out)
+    assert ops.device_status() == 0
