@@ -87,6 +87,15 @@ __device__ __forceinline__ void store32(T *dst, const float (&v)[32]) {
   st_global_v8(dst + 16, pk + 8);
 }
 
+// 16 values -> 8 packed pairs -> one 256-bit store.
+template <typename T>
+__device__ __forceinline__ void store16(T *dst, const float (&v)[16]) {
+  uint32_t pk[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) pk[e] = pack2<T>(v[2 * e], v[2 * e + 1]);
+  st_global_v8(dst, pk);
+}
+
 template <typename T>
 struct QkvEpilogue {
   T *q_out;                 // [M, num_heads, head_dim]
@@ -98,6 +107,94 @@ struct QkvEpilogue {
   float rms_eps;
   int32_t num_heads, num_kv_heads, head_dim, num_blocks, block_size, max_position;
   static constexpr bool kChunked = false;  // RoPE and the q/k norms need whole heads
+  static constexpr bool kSplitUnits = true;  // the split-K form uses unit() below
+
+  // Where this row's values of global head `gh` go (null: nothing to write), reporting bad
+  // positions and slots; `pos` / `slot` are the row's.
+  __device__ T *destination(int row, int gh, bool is_q, bool is_k, int pos, int slot,
+                            const GemmShape &s) const {
+    if (row >= s.M) return nullptr;
+    if ((is_q || is_k) && !(pos >= 0 && pos < max_position)) {
+      report(FA_DEVERR_POSITION);
+      return nullptr;
+    }
+    if (is_q) return q_out + (size_t(row) * num_heads + gh) * head_dim;
+    if (slot >= 0) {
+      const int blk = slot / block_size, off = slot % block_size;
+      if (blk < num_blocks) {
+        const int kvh = gh - num_heads - (is_k ? 0 : num_kv_heads);
+        return (is_k ? k_cache : v_cache) +
+               ((size_t(blk) * num_kv_heads + kvh) * block_size + off) * head_dim;
+      }
+      report(FA_DEVERR_SLOT);
+    } else if (slot < -1) {
+      report(FA_DEVERR_SLOT);
+    }
+    return nullptr;
+  }
+
+  // Split-K form, for a tile whose few valid rows would leave most epilogue threads idle: one
+  // unit = 16 rotate-half pairs (columns i..i+15 and i+d/2..) of one head of one row, BN / 32
+  // units per row. The summed row sits in shared memory (acc.row), so a unit reads the whole
+  // head for the norm itself. Same arithmetic, in the same order, as operator().
+  template <int BN, class Acc>
+  __device__ void unit(const Acc &acc, int row, int col0, int u, const GemmShape &s) const {
+    const int half = head_dim / 2;
+    const int per_head = half / 16;
+    const int hl = u / per_head, i0 = (u % per_head) * 16;
+    const int f0 = col0 + hl * head_dim;
+    if (row >= s.M || f0 >= s.N) return;
+    const int gh = f0 / head_dim;
+    const bool is_q = gh < num_heads, is_k = !is_q && gh < num_heads + num_kv_heads;
+    const int pos = positions[row], slot = slots[row];
+    T *dst = destination(row, gh, is_q, is_k, pos, slot, s);
+    if (dst == nullptr) return;
+    const T *nw = is_q ? q_norm : (is_k ? k_norm : nullptr);
+    const float *r = acc.row + hl * head_dim;
+    float inv_rms = 1.f;
+    if (nw) {
+      float ss = 0.f;
+      for (int c = 0; c < head_dim; c += 32)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float x = r[c + e] + (bias ? to_f32(bias[f0 + c + e]) : 0.f);
+          ss = fmaf(x, x, ss);
+        }
+      inv_rms = rsqrtf(ss / float(head_dim) + rms_eps);
+    }
+    float a[16], b[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      a[e] = r[i0 + e];
+      b[e] = r[half + i0 + e];
+      if (bias) {
+        a[e] += to_f32(bias[f0 + i0 + e]);
+        b[e] += to_f32(bias[f0 + half + i0 + e]);
+      }
+      if (nw) {
+        a[e] *= inv_rms * to_f32(nw[i0 + e]);
+        b[e] *= inv_rms * to_f32(nw[half + i0 + e]);
+      }
+    }
+    if (is_q || is_k) {
+      const float4 *cp = reinterpret_cast<const float4 *>(rope_cos + size_t(pos) * half + i0);
+      const float4 *sp = reinterpret_cast<const float4 *>(rope_sin + size_t(pos) * half + i0);
+#pragma unroll
+      for (int e4 = 0; e4 < 4; ++e4) {
+        const float4 c4 = cp[e4], s4 = sp[e4];
+        const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int e = e4 * 4 + j;
+          const float x1 = a[e], x2 = b[e];
+          a[e] = x1 * cs[j] - x2 * sn[j];
+          b[e] = x2 * cs[j] + x1 * sn[j];
+        }
+      }
+    }
+    store16<T>(dst + i0, a);
+    store16<T>(dst + half + i0, b);
+  }
 
   // One row (token) of a 128 x BN tile: BN / head_dim whole heads starting at column col0.
   template <int BN, class Acc>
@@ -200,6 +297,7 @@ struct ResidualEpilogue {
   T *out;                 // [M, N]
   const T *residual;      // [M, N] or null
   static constexpr bool kChunked = true;  // 32-column chunks are independent
+  static constexpr bool kSplitUnits = false;
 
   __device__ void apply32(float (&v)[32], int row, int col, const GemmShape &s) const {
     const size_t base = size_t(row) * s.N + col;
@@ -248,6 +346,7 @@ struct ResidualEpilogue {
 struct F32Epilogue {
   float *out;  // [M, N], N % 32 == 0, 16-byte aligned
   static constexpr bool kChunked = true;  // 32-column chunks are independent
+  static constexpr bool kSplitUnits = false;
 
   __device__ void apply32(const float (&v)[32], int row, int col, const GemmShape &s) const {
     float4 *d = reinterpret_cast<float4 *>(out + size_t(row) * s.N + col);
@@ -688,6 +787,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int u = t; u < rows * kChunks; u += 128) {
           const int row = row0 + u / kChunks;
           epi.chunk(LocalAcc{part + row * kPitch}, m * 128 + row, n * BN, u % kChunks, s);
+        }
+      } else if constexpr (Epi::kSplitUnits) {
+        // BN / 32 units per row (each 16 rotate-half pairs of one head) over all 128 threads.
+        constexpr int kUnits = BN / 32;
+        for (int u = t; u < rows * kUnits; u += 128) {
+          const int row = row0 + u / kUnits;
+          epi.template unit<BN>(LocalAcc{part + row * kPitch}, m * 128 + row, n * BN,
+                                u % kUnits, s);
         }
       } else if (t < rows) {
         const int row = row0 + t;
