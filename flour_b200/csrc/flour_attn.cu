@@ -381,12 +381,12 @@ fa_status launch_prefill_t(const fa::PrefillParams &p, const CUtensorMap &tq, co
                            const CUtensorMap &tv, int grid_x, cudaStream_t stream) {
   using S = fa::PrefillSmem;
   auto kern = fa::paged_prefill_kernel<T, kRef>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAllocMax);
   if (e != cudaSuccess) return fail(FA_ECUDA, "prefill: set smem attribute: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(grid_x));
   cfg.blockDim = dim3(fa::kPfThreads);
-  cfg.dynamicSmemBytes = S::kAlloc;
+  cfg.dynamicSmemBytes = S::alloc(p.num_seqs);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];  // programmatic dependent launch: setup overlaps the predecessor
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -84,8 +84,7 @@ struct PrefillSmem {
   static constexpr int kQOff = 0;                             // Q_A, Q_B
   static constexpr int kKOff = 2 * kTile;                     // K ring
   static constexpr int kVOff = kKOff + kPfStages * kTile;     // V ring
-  static constexpr int kOffsOff = kVOff + kPfStages * kTile;  // chunk prefix sums [kPfMaxSeqs+1]
-  static constexpr int kItemOff = kOffsOff + ((kPfMaxSeqs + 1) * 4 + 63) / 64 * 64;
+  static constexpr int kItemOff = kVOff + kPfStages * kTile;
   static constexpr int kXchOff = kItemOff + 2 * int(sizeof(PfItem));  // f32 [2 X][2 halves][128]
   static constexpr int kBarOff = kXchOff + 2 * 2 * 128 * 4;
   // barrier indices (pairs are indexed by Q tile X or ring stage)
@@ -95,8 +94,11 @@ struct PrefillSmem {
                        IFULL = ODONE + 2, IEMPTY = IFULL + 2, DRAIN = IEMPTY + 2,
                        NBARS = DRAIN + 1;
   static constexpr int kMiscOff = kBarOff + NBARS * 8;
-  static constexpr int kBytes = kMiscOff + 64;
-  static constexpr int kAlloc = kBytes + 1024;
+  // Chunk prefix sums [num_seqs + 1] last, so a launch requests only what its batch needs (the
+  // rest of the SM's shared memory stays free for other kernels' CTAs).
+  static constexpr int kOffsOff = kMiscOff + 64;
+  static constexpr int alloc(int num_seqs) { return kOffsOff + (num_seqs + 1) * 4 + 1024; }
+  static constexpr int kAllocMax = kOffsOff + (kPfMaxSeqs + 1) * 4 + 1024;
 };
 
 // Named-barrier helpers for a pair of warps (64 threads). pair_all is a barrier that also ANDs
