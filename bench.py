@@ -549,7 +549,7 @@ def run_ours(args):
                        "hbm_frac_of_measured_peak": round(value / world / hbm_peak, 4)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                         "traffic": traffic, "kernel": "paged_decode_kernel<bf16,128,3>",
+                         "traffic": traffic, "kernel": "paged_decode_kernel<bf16,128,2>",
                          "launch_ms": round(launch_ms, 5),
                          "frac_uses": "launch_ms: the decode kernel's average launch duration "
                                       "inside the graph-replayed timed region (step time / 32)",

@@ -123,7 +123,7 @@ __device__ __forceinline__ void store_out(const DecodeParams &p, int b, int hq, 
 }
 
 template <typename T, int HD, int NSTAGE>
-__global__ void __launch_bounds__(kDecodeThreads, 2)
+__global__ void __launch_bounds__(kDecodeThreads, 3)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v) {

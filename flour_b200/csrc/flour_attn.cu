@@ -114,23 +114,27 @@ fa_status make_q_map(CUtensorMap *map, const void *q, int total_q, int num_heads
 // ---- decode planning --------------------------------------------------------------------
 
 constexpr int kSmCount = 148;
-constexpr int kDecodeCtasPerSm = 2;
+// The split plan's CTA target: 12 per SM (see plan_decode). Three decode CTAs are resident per
+// SM (2-stage rings), so this is four resident waves.
+constexpr int kDecodeCtasPerSmTarget = 12;
 
 struct DecodePlan {
   int pages_per_split = 0;
   int max_splits = 0;
 };
 
-// Split the context so that about six waves of CTAs cover the whole GPU, with at least 32
-// pages per split (8 per warp) and at most kDecodeMaxPagesPerSplit. Six waves measured best on
-// B200 for C2 (U[512, 4096] contexts): 4 leaves a ragged last wave, 8+ pays more per-split
-// overhead than it saves. The 32-page floor matters for small batches of short contexts, where
-// the six-wave target would cut splits of 16 pages whose fixed per-CTA cost dominates (59
-// sequences of 1419 tokens, Qwen2-7B heads: 54.7 -> 45.0 us; C2 unchanged).
+// Split the context so that about 12 CTAs per SM cover the whole GPU, with at least 32 pages per
+// split (8 per warp) and at most kDecodeMaxPagesPerSplit. That target measured best on B200 for
+// C2 (U[512, 4096] contexts) with two resident CTAs per SM (six waves: four left a ragged last
+// wave, eight or more paid more per-split overhead than they saved), and kept its edge once three
+// became resident (C2 6015 -> 6185 GB/s; a 3-per-SM target of 18 CTAs per SM reached only 6090).
+// The 32-page floor matters for small batches of short contexts, where the target would cut
+// splits of 16 pages whose fixed per-CTA cost dominates (59 sequences of 1419 tokens, Qwen2-7B
+// heads: 54.7 -> 45.0 us; C2 unchanged).
 bool plan_decode(int num_seqs, int num_kv_heads, int max_context_len, DecodePlan *out) {
   const int max_pages = (max_context_len + fa::kPage - 1) / fa::kPage;
   const long units = long(num_seqs) * num_kv_heads;
-  const long target = long(kSmCount) * kDecodeCtasPerSm * 6;
+  const long target = long(kSmCount) * kDecodeCtasPerSmTarget;
   const long want = std::max(1L, (target + units - 1) / units);
   int pps = int((max_pages + want - 1) / want);
   pps = std::max(pps, 32);
@@ -191,7 +195,11 @@ fa_status launch_decode_t(const fa::DecodeParams &p, const CUtensorMap &tk, cons
   return check_launch("paged_decode");
 }
 
-constexpr int kDecodeStages = 3;
+// Two ring stages per warp keep each decode CTA at 66 KB of shared memory, so three are resident
+// per SM (with three stages only two fit): the same pages in flight per SM, and a third CTA's
+// streaming hides the others' prologues and split-K merges (C2 6015 -> 6185 GB/s; C5's 59-sequence
+// decode 38.2 -> 35.2 us per layer).
+constexpr int kDecodeStages = 2;
 
 // Split-K merge tickets must be zero when a decode launch starts. Every launch returns its own
 // tickets to zero, but a caller workspace reused with another shape may hold split-K partials
