@@ -28,17 +28,15 @@ namespace fa {
 constexpr int kGemmBK = 64;          // K per ring stage: one 128-byte swizzled row per operand row
 constexpr int kGemmThreads = 192;    // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
 
-// AROWS = 64 (split-K with M <= 64 only): the A stage holds 64 rows. The ring then takes 4 stages
-// (96 KB), so a CTA needs half an SM's shared memory and the clusters of a larger split fit in
-// one wave (decode-batch QKV 20.9 -> 18.5 us, o_proj 14.9 -> 12.9 us against 8 stages; 3 and 6
-// stages measured in between). The M = 128 MMA still reads 128 A rows; rows
+// AROWS = 64 (split-K with M <= 64 only): the A stage holds 64 rows, so the ring takes 8 stages
+// instead of 6 (more weight bytes in flight per SM). The M = 128 MMA still reads 128 A rows; rows
 // 64-127 then fall on the same stage's B bytes and only feed accumulator rows >= 64, which the
 // epilogue never stores. The kernel refuses (FA_DEVERR_LAUNCH, no work) a shape with M > 64.
 template <int BN, int AROWS = 128>
 struct GemmCfg {
   static_assert(BN == 128 || BN == 256, "BN is 128 or 256");
   static_assert(AROWS == 128 || (AROWS == 64 && BN == 128), "64-row A stages only at BN = 128");
-  static constexpr int kStages = BN == 256 ? 4 : (AROWS == 64 ? 4 : 6);
+  static constexpr int kStages = BN == 256 ? 4 : (AROWS == 64 ? 8 : 6);
   static constexpr int kABytes = AROWS * kGemmBK * 2;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
