@@ -534,15 +534,15 @@ int gemm_bn(int M, int N) {
   return cols128 * 10 < cols256 * 9 ? 128 : 256;
 }
 
-template <typename T, int BN, class Epi>
-fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, const void *b,
-                        int32_t dt, cudaStream_t stream, const char *who) {
-  using C = fa::GemmCfg<BN>;
+template <typename T, int BN, int AROWS, class Epi>
+fa_status launch_gemm_rows(int M, int N, int K, const Epi &epi, const void *a, const void *b,
+                           int32_t dt, cudaStream_t stream, const char *who) {
+  using C = fa::GemmCfg<BN, AROWS>;
   fa::GemmShape s{M, N, K, (M + 127) / 128, (N + BN - 1) / BN};
   CUtensorMap ta, tb;
-  if (fa_status st = make_gemm_map(&ta, a, M, K, dt, 128, who); st != FA_OK) return st;
+  if (fa_status st = make_gemm_map(&ta, a, M, K, dt, AROWS, who); st != FA_OK) return st;
   if (fa_status st = make_gemm_map(&tb, b, N, K, dt, BN, who); st != FA_OK) return st;
-  auto kern = fa::gemm_tn_kernel<T, BN, Epi>;
+  auto kern = fa::gemm_tn_kernel<T, BN, Epi, AROWS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   if (e != cudaSuccess) return fail(FA_ECUDA, "%s: set smem attribute: %s", who, cudaGetErrorString(e));
   const int grid = int(std::min<int64_t>(sm_count(), int64_t(s.tiles_m) * s.tiles_n));
@@ -561,6 +561,16 @@ fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, cons
   e = cudaLaunchKernelEx(&cfg, kern, s, epi, ta, tb);
   if (e != cudaSuccess) return fail(FA_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return check_launch(who);
+}
+
+// Batches of <= 64 rows on 128-wide tiles load 64-row A boxes: 8 ring stages instead of 6, more
+// weight bytes in flight (the logits readback of a decode batch).
+template <typename T, int BN, class Epi>
+fa_status launch_gemm_t(int M, int N, int K, const Epi &epi, const void *a, const void *b,
+                        int32_t dt, cudaStream_t stream, const char *who) {
+  if constexpr (BN == 128)
+    if (M <= 64) return launch_gemm_rows<T, 128, 64>(M, N, K, epi, a, b, dt, stream, who);
+  return launch_gemm_rows<T, BN, 128>(M, N, K, epi, a, b, dt, stream, who);
 }
 
 // Split-K over a cluster of `ranks` CTAs per 128 x 128 tile (one tile per cluster).

@@ -28,8 +28,9 @@ namespace fa {
 constexpr int kGemmBK = 64;          // K per ring stage: one 128-byte swizzled row per operand row
 constexpr int kGemmThreads = 192;    // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
 
-// AROWS = 64 (split-K with M <= 64 only): the A stage holds 64 rows, so the ring takes 8 stages
-// instead of 6 (more weight bytes in flight per SM). The M = 128 MMA still reads 128 A rows; rows
+// AROWS = 64 (M <= 64 only: the split-K form, and the persistent form at BN = 128, e.g. the
+// logits readback of a decode batch): the A stage holds 64 rows, so the ring takes 8 stages
+// instead of 6 (more weight bytes in flight per SM; logits at 64 rows 187.1 -> 184.5 us). The M = 128 MMA still reads 128 A rows; rows
 // 64-127 then fall on the same stage's B bytes and only feed accumulator rows >= 64, which the
 // epilogue never stores. The kernel refuses (FA_DEVERR_LAUNCH, no work) a shape with M > 64.
 template <int BN, int AROWS = 128>
@@ -419,12 +420,12 @@ __global__ void __launch_bounds__(kNormThreads)
 
 // ---- the persistent GEMM ---------------------------------------------------------------------
 
-template <typename T, int BN, class Epi>
+template <typename T, int BN, class Epi, int AROWS = 128>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_kernel(const __grid_constant__ GemmShape s, const __grid_constant__ Epi epi,
                    const __grid_constant__ CUtensorMap tm_a,
                    const __grid_constant__ CUtensorMap tm_b) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, AROWS>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -436,6 +437,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles = s.tiles_m * s.tiles_n;
   const int num_k = (s.K + kGemmBK - 1) / kGemmBK;
+  if (AROWS < 128 && s.M > AROWS) {  // uniform over the grid: every CTA leaves before any barrier
+    if (tid == 0 && blockIdx.x == 0) report(FA_DEVERR_LAUNCH);
+    return;
+  }
 
   if (tid == 0) {
     for (int i = 0; i < C::NBARS; ++i)
