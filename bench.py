@@ -604,7 +604,7 @@ def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_
     """Per step: the host hands per-layer q and new k/v (pinned) plus the step's metadata
     (block tables, context lengths); the library writes the cache and attends (one
     fa_paged_decode_append per layer) and the host reads every layer's output back. Copies run on
-    a side stream, one layer ahead."""
+    a side stream ahead of the decodes."""
     B = batch.num_seqs
     gen = torch.Generator().manual_seed(7)
     hq = [torch.randn((B, h.num_heads, h.head_dim), generator=gen).to(torch.bfloat16).pin_memory()
@@ -642,7 +642,11 @@ def run_e2e(args, torch, ops, batch, h, scale, slots, ws, dev, stream, kv_bytes_
                 ev_in.append(e)
         ev_out = []
         for l in range(NUM_LAYERS):
-            stream.wait_event(ev_in[l])
+            # The copies run far ahead of the decodes, so the decode stream waits only at layers
+            # 0, 1, 2, 4, 8 and 16, each wait covering the inputs of layers [l, 2l): fewer waits
+            # between consecutive decode launches (e2e +1.2 % against a wait before every layer).
+            if l == 0 or (l & (l - 1)) == 0:
+                stream.wait_event(ev_in[min(2 * l, NUM_LAYERS) - 1 if l else 0])
             ops.paged_decode_append(dq[l], batch.k_caches[l], batch.v_caches[l], dk[l], dv[l],
                                     d_bt, d_ctx, h.n_rep, scale, batch.max_context_len, ws,
                                     out=do[l])
