@@ -296,9 +296,14 @@ def c5_plan(seed: int, n: int = 512, prefill_frac: float = 0.1):
 
 def mixed_partition(costs, is_prefill, parts: int, overlap: float = 0.5) -> list[list[int]]:
     """Sequence sharding for a step whose decode and prefill sub-batches run on two streams of
-    each GPU: a GPU with prefill time P and decode time D takes about max(P, D) + overlap *
+    each GPU: a GPU with prefill time P and decode time D is estimated at max(P, D) + overlap *
     min(P, D). Prompts are placed first (longest-first, the larger and coarser work), then each
-    decode sequence, longest first, goes where that estimate grows least."""
+    decode sequence, longest first, goes where that estimate grows least.
+
+    The estimate is a balancing model, not the measured overlap: on B200 the C5 shares' two
+    streams overlap by only 4-8 us per layer (the persistent prefill kernel holds every SM while
+    it runs), while the per-token decode cost in c5_plan is above the measured rate by a similar
+    margin; with overlap 0.5 the eight measured N=8 shares land within 3 % of each other."""
     costs = np.asarray(costs, dtype=np.float64)
     is_prefill = np.asarray(is_prefill, dtype=bool)
     pf = np.flatnonzero(is_prefill)
