@@ -91,6 +91,38 @@ def test_workspace_sizes():
     assert L.fa_paged_attention_workspace_size(0, 32, 8, 128, 4096, 1) == 0
 
 
+def _decode_plan_workspace(num_seqs, num_heads, num_kv_heads, head_dim, max_context_len):
+    """The decode split plan and its workspace, restated: about 12 CTAs per SM over 148 SMs for
+    the longest context, 32 to 256 pages per split rounded up to a multiple of 4; then merge
+    tickets, per-split LSE and per-split f32 partial outputs, each region 256-byte aligned."""
+    r256 = lambda x: (x + 255) // 256 * 256
+    max_pages = -(-max_context_len // 16)
+    units = num_seqs * num_kv_heads
+    want = max(1, -(-148 * 12 // units))
+    pps = min((max(-(-max_pages // want), 32) + 3) // 4 * 4, 256)
+    splits = max(-(-max_pages // pps), 1)
+    if splits <= 1:
+        return pps, splits, 0
+    lse_off = r256(num_seqs * num_kv_heads * 4)
+    o_off = lse_off + r256(num_seqs * num_heads * splits * 4)
+    return pps, splits, o_off + num_seqs * num_heads * splits * head_dim * 4
+
+
+@pytest.mark.parametrize("shape, pps, splits", [
+    ((64, 32, 8, 128, 4096), 64, 4),      # C2 batch
+    ((59, 28, 4, 128, 6438), 52, 8),      # a C5 rank's decode share at N=8
+    ((59, 28, 4, 128, 1419), 32, 3),      # short uniform contexts: the 32-page floor
+    ((16, 32, 8, 128, 32768), 148, 14),   # C4 long context
+    ((4, 32, 8, 128, 256), 32, 1),        # one split: no workspace
+])
+def test_decode_split_plan_is_pinned(shape, pps, splits):
+    """The measured-best split plan (C2, C5 shares, short batches, C4) is what the library
+    sizes its workspace for; a retuned plan must change these cases on purpose."""
+    got_pps, got_splits, expect = _decode_plan_workspace(*shape)
+    assert (got_pps, got_splits) == (pps, splits)
+    assert lib().fa_paged_attention_workspace_size(*shape, 1) == expect
+
+
 def test_decode_workspace_too_small_is_rejected_without_launch():
     L = lib()
     ly = layer(nb=4096, kvh=8, bs=16, d=128)
