@@ -286,7 +286,13 @@ class BatchMetadata:
 
 def build_batch(tables: list[BlockTable], q_lens: list[int], device) -> BatchMetadata:
     """Batched form of the per-sequence bookkeeping (cache.rs:71-96): one int32 block-table
-    row per sequence, its live length, and the slots of its trailing q_len new tokens."""
+    row per sequence, its live length, and the slots of its trailing q_len new tokens. Raises the
+    C++ host's errors for lists of different lengths and for a q_len outside [0, len]."""
+    if len(tables) != len(q_lens):
+        raise ValueError("build_batch: tables and q_lens differ in length")
+    for t, n in zip(tables, q_lens):
+        if n < 0 or n > t.len():
+            raise ValueError("build_batch: q_len exceeds the sequence length")
     B = len(tables)
     max_blocks = max(1, max(len(t.blocks()) for t in tables)) if tables else 1
     bt = torch.zeros((B, max_blocks), dtype=torch.int32)

@@ -286,6 +286,25 @@ void build_batch_packs_tables_lengths_and_slots() {
   expect_error([&] { build_batch({&b}, {6}); }, "q_len exceeds the sequence length");
 }
 
+void build_batch_edge_cases() {
+  const BatchMetadata e = build_batch({}, {});
+  EXPECT(e.num_seqs == 0 && e.max_blocks_per_seq == 1 && e.total_q == 0);
+  EXPECT(e.block_tables.empty() && e.context_lens.empty() && e.slot_mapping.empty());
+  EXPECT(e.cu_seqlens_q == std::vector<int32_t>({0}));
+  EXPECT(e.max_context_len == 0 && e.max_seqlen_q == 0);
+  BlockTable a(16), b(16);
+  a.push_block(3);
+  a.advance(10);
+  b.push_block(5);
+  b.push_block(6);
+  b.advance(17);
+  const BatchMetadata m = build_batch({&a, &b}, {0, 2});  // a sequence with no new tokens
+  EXPECT(m.cu_seqlens_q == std::vector<int32_t>({0, 0, 2}) && m.total_q == 2);
+  EXPECT(m.slot_mapping == std::vector<int32_t>({5 * 16 + 15, 6 * 16 + 0}));
+  EXPECT(m.block_tables == std::vector<int32_t>({3, 0, 5, 6}) && m.max_seqlen_q == 2);
+  expect_error([&] { build_batch({&a, &b}, {1}); }, "tables and q_lens differ in length");
+}
+
 // ---- GPU cases -------------------------------------------------------------------------------
 
 void paged_pool_write_then_gather_round_trips() {  // paged.rs:288-306
@@ -403,6 +422,7 @@ int main(int argc, char **argv) {
   run("clear_prefix_cache_disables_reuse", clear_prefix_cache_disables_reuse);
   run("clear_prefix_cache_releases_registry_only_blocks_to_the_pool", clear_prefix_cache_releases_registry_only_blocks_to_the_pool);
   run("build_batch_packs_tables_lengths_and_slots", build_batch_packs_tables_lengths_and_slots);
+  run("build_batch_edge_cases", build_batch_edge_cases);
   if (gpu) {
     if (device_count() < 1) {
       std::printf("FAIL no CUDA device for --gpu\n");

@@ -73,6 +73,30 @@ def test_build_batch_matches_per_sequence_slots():
     assert meta.max_context_len == 40 and meta.max_seqlen_q == 8
 
 
+def test_build_batch_edge_cases():
+    """Empty batch, a sequence with no new tokens, and the C++ host's two errors."""
+    empty = build_batch([], [], "cpu")
+    assert empty.block_tables.shape == (0, 1) and empty.context_lens.tolist() == []
+    assert empty.cu_seqlens_q.tolist() == [0] and empty.slot_mapping.tolist() == []
+    assert empty.max_context_len == 0 and empty.max_seqlen_q == 0
+    a, b = BlockTable(16), BlockTable(16)
+    a.push_block(3)
+    a.advance(10)
+    b.push_block(5)
+    b.push_block(6)
+    b.advance(17)
+    meta = build_batch([a, b], [0, 2], "cpu")
+    assert meta.cu_seqlens_q.tolist() == [0, 0, 2]
+    assert meta.slot_mapping.tolist() == [5 * 16 + 15, 6 * 16 + 0]
+    assert meta.block_tables.tolist() == [[3, 0], [5, 6]] and meta.max_seqlen_q == 2
+    with pytest.raises(ValueError, match="differ in length"):
+        build_batch([a, b], [1], "cpu")
+    with pytest.raises(ValueError, match="q_len exceeds the sequence length"):
+        build_batch([a], [11], "cpu")
+    with pytest.raises(ValueError, match="q_len exceeds the sequence length"):
+        build_batch([a], [-1], "cpu")
+
+
 def test_lpt_partition_balances_lognormal_contexts():
     ctx = c5_contexts(5)
     parts = lpt_partition(ctx, 8)
