@@ -95,6 +95,10 @@ class BlockTable:
         self._len += n
 
     def slot(self, pos: int) -> int:
+        # Positions are unsigned in the reference (paged.rs:114-116 indexes with a usize): a
+        # negative one is out of range like one past the last block, not the last block's slot.
+        if pos < 0:
+            raise IndexError(f"slot position {pos} out of range")
         return self._blocks[pos // self._block_size] * self._block_size + pos % self._block_size
 
     def slots(self, start: int, end: int) -> list[int]:

@@ -44,6 +44,11 @@ def test_block_table_maps_logical_positions_to_physical_slots():  # paged.rs:377
     t.advance(3)
     assert t.len() == 3
     assert t.slots(0, 3) == [10, 11, 6]
+    # Past the last block or before the first: out of range (a panic in the reference).
+    with pytest.raises(IndexError):
+        t.slot(4)
+    with pytest.raises(IndexError):
+        t.slot(-1)
 
 
 def test_block_table_exposes_blocks_and_clears():  # paged.rs:396-411
