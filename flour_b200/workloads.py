@@ -20,7 +20,7 @@ torch generator seeded with the same value on the target device.
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 import torch

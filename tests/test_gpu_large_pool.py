@@ -10,7 +10,6 @@ import pytest
 import torch
 
 from flour_b200 import ops
-from flour_b200.workloads import LLAMA8B
 
 from _util import f32, max_abs, oracle_attention
 

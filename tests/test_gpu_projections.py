@@ -189,7 +189,6 @@ def test_fused_layer_matches_unfused_path(device):
     """x -> fused QKV (+cache) -> paged prefill -> fused o_proj + residual equals the same layer
     built from the oracle pieces (the whole of CausalSelfAttention::forward + the residual)."""
     import oracle
-    from flour_b200.workloads import to_numpy
     T, hidden, Hq, Hkv, d = 96, 512, 8, 2, 128
     c = make_qkv(device, T, hidden, Hq, Hkv, d, seed=12, num_blocks=16)
     # one sequence of T tokens at positions 0..T-1 in blocks 0..5

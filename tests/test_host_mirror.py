@@ -3,7 +3,6 @@ tests (src/models/common/paged.rs:343-411) and the batch metadata builder."""
 
 import numpy as np
 import pytest
-import torch
 
 from flour_b200.paged import BlockAllocator, BlockTable, build_batch
 from flour_b200.workloads import (QWEN7B, c5_contexts, c5_plan, lpt_partition, make_c3,

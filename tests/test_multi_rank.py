@@ -14,7 +14,6 @@ import traceback
 from datetime import timedelta
 
 import numpy as np
-import pytest
 
 WORLD = 2
 

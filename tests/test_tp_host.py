@@ -10,7 +10,6 @@
     calls so no GPU is needed.
 """
 
-import ctypes
 import multiprocessing as mp
 import os
 import socket
